@@ -1,0 +1,444 @@
+#!/usr/bin/env python
+"""Batch-one SwiGLU FFN decode layer (4096 -> 14336) on B200: us per layer and % of HBM peak.
+
+One step = one full layer (gate = Wg x + bg, up = Wu x + bu, h = SiLU(gate) * up,
+y = Wd h + bd + x; fp16 weights, fp32 accumulation, fp16 h, fp32 y) on seeded
+synthetic inputs, weights cycling through rotating copies whose total exceeds
+twice the 126 MB L2, so every step streams its weights from HBM.
+
+* N = 1: the two product kernels (gate, down) on one B200.
+* N > 1 (torchrun, one rank per GPU): tensor parallel. Wg/Wu split by
+  intermediate row, Wd by its K dimension; one NCCL all-reduce of the fp32 y,
+  then bias + residual once. Each rank's step is captured in a CUDA graph.
+
+Prints ONE JSON line on rank 0. ``--impl reference`` times the reference's own
+CPU path (its include/contract.hpp matvec, compiled under oracle/_ref) on the
+host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "cuda-kernel_b200"))
+
+METRIC = "SwiGLU FFN µs/layer and % of HBM peak, batch 1 (4096→14336), 1/2/4/8 B200"
+UNIT = "us/layer"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--hidden", type=int, default=4096)
+    p.add_argument("--intermediate", type=int, default=14336)
+    p.add_argument("--gate-config", type=int, default=0, help="registry id (0 = tune)")
+    p.add_argument("--down-config", type=int, default=0, help="registry id (0 = tune)")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-cublas", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# --------------------------------------------------------------- reference arm
+
+def reference_arm(args) -> None:
+    """The reference's CPU implementation of the layer on all host threads (rank 0 only)."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT))
+    import oracle  # the checker package: used here only as the timed reference arm
+    H, I = args.hidden, args.intermediate
+    threads = len(os.sched_getaffinity(0))
+    w = oracle.normal_workload(0, H, I)
+    if oracle.ref_available():
+        kind = "reference"
+        run = lambda: oracle.ref_ffn(w, threads=threads)  # noqa: E731
+    else:
+        kind = "port"
+        threads = 1
+        run = lambda: oracle.ffn(w)  # noqa: E731
+    for _ in range(max(args.warmup, 0)):
+        run()
+    samples = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s = time.perf_counter()
+        run()
+        samples.append(time.perf_counter() - s)
+    total = time.perf_counter() - t0
+    us = total / args.steps * 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, f64 accumulate (CPU)", "data": "synthetic",
+        "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
+                   "parallelism": "host threads", "seed": 0},
+        "cpu_baseline": {"value": us, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} full {H}->{I} layers (decode::matvec x3 + SiLU + residual), "
+                                   f"rows split over {threads} threads",
+                         "median_step_us": statistics.median(samples) * 1e6},
+        "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+
+def make_weights(torch, H, I, copies, device, seed=0):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def normal(shape, scale):
+        return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * scale).half()
+
+    sets = []
+    for _ in range(copies):
+        sets.append({"wg": normal((I, H), 1 / math.sqrt(H)), "wu": normal((I, H), 1 / math.sqrt(H)),
+                     "wd": normal((H, I), 1 / math.sqrt(I))})
+    common = {"x": normal((H,), 1.0), "bg": normal((I,), 0.02), "bu": normal((I,), 0.02), "bd": normal((H,), 0.02)}
+    return sets, common
+
+
+def time_kernel(torch, fn, reps, stream):
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(reps):
+        fn(i)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) * 1e3 / reps
+
+
+def tune(torch, binding, launch_gate, launch_down, ids, stream, reps=8):
+    """Pick the fastest gate and down geometry by median over rotating copies."""
+    best = {}
+    for name, launch in (("gate", launch_gate), ("down", launch_down)):
+        times = {}
+        for cid in ids:
+            launch(cid, 0)
+            torch.cuda.synchronize()
+            samples = [time_kernel(torch, lambda i, c=cid: launch(c, i), reps, stream) for _ in range(3)]
+            times[cid] = statistics.median(samples)
+        best[name] = min(times, key=times.get)
+        best[name + "_times"] = times
+    return best
+
+
+def traffic_from_profile(kernel_tag: str, H: int, I: int):
+    """DRAM bytes per launch recorded by the committed ncu summary for this kernel/workload, if any."""
+    path = ROOT / "profiles" / f"{kernel_tag}_{H}x{I}.txt"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(sets, common, H, I, budget_s):
+    """The reference's CPU path (oracle/_ref, one thread) on a bounded sample of whole layers."""
+    sys.path.insert(0, str(ROOT))
+    import oracle  # the checker package: used here only as the timed CPU baseline
+    w = {k: sets[0][k].cpu().numpy() for k in ("wg", "wu", "wd")}
+    w.update({k: common[k].cpu().numpy() for k in ("x", "bg", "bu", "bd")})
+    if oracle.ref_available():
+        kind, run = "reference", (lambda: oracle.ref_ffn(w, threads=1))
+    else:
+        kind, run = "port", (lambda: oracle.ffn(w))
+    run()  # warm caches / page in
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 1000:
+            break
+    return {"value": el / n * 1e6, "unit": UNIT, "cores": 1, "kind": kind,
+            "sample": f"{n} full {H}->{I} layers on 1 host thread (decode::matvec x3 + SiLU + residual, "
+                      f"as src/benchmark.cu:131-141), {el:.1f} s"}
+
+
+def ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+    from swiglu_b200 import binding, _lib, intensity
+    from swiglu_b200.clocks import ClockSampler
+
+    world, rank, local = dist_env()
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    _lib.lib()  # fail loudly now if the native library is missing
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    H, I = args.hidden, args.intermediate
+    if I % world:
+        raise SystemExit("intermediate size must divide by the GPU count")
+    shard = I // world
+    layer = intensity.layer(H, I)
+    if world == 1:
+        rank_bytes = layer["bytes"]
+        gate_bytes = layer["gate"]["bytes"]
+    else:
+        tpb = intensity.tp_rank(H, I, world)
+        rank_bytes = tpb["bytes"]
+        gate_bytes = tpb["gate"]["bytes"]
+    weight_bytes_rank = 3 * H * shard * 2
+    copies = max(2, math.ceil(2 * L2_BYTES / weight_bytes_rank) + 1)
+
+    # All work runs on one dedicated stream (graph capture cannot use the legacy default stream).
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+
+    # Full weights are drawn on every rank from the same seed, then each rank keeps its shard.
+    full_sets, common = make_weights(torch, H, I, copies, device)
+    r0, r1 = rank * shard, (rank + 1) * shard
+    sets = []
+    for s in full_sets:
+        sets.append({"wg": s["wg"][r0:r1].contiguous(), "wu": s["wu"][r0:r1].contiguous(),
+                     "wd": s["wd"][:, r0:r1].contiguous()})
+    bg, bu = common["bg"][r0:r1].contiguous(), common["bu"][r0:r1].contiguous()
+    x, bd = common["x"], common["bd"]
+    w0 = full_sets[0]
+    del full_sets
+    torch.cuda.synchronize()
+
+    h = torch.empty(shard, dtype=torch.float16, device=device)
+    y = torch.empty(H, dtype=torch.float32, device=device)
+    L = _lib.lib()
+
+    def launch_gate(cid, i):
+        s = sets[i % copies]
+        _lib.check(L.swb_gate(cid, s["wg"].data_ptr(), s["wu"].data_ptr(), x.data_ptr(), bg.data_ptr(),
+                              bu.data_ptr(), h.data_ptr(), shard, H, 0, sp))
+
+    if world == 1:
+        def launch_down(cid, i):
+            s = sets[i % copies]
+            _lib.check(L.swb_project(cid, s["wd"].data_ptr(), h.data_ptr(), bd.data_ptr(), x.data_ptr(),
+                                     y.data_ptr(), H, shard, _lib.SWB_RESIDUAL, sp))
+    else:
+        def launch_down(cid, i):
+            s = sets[i % copies]
+            _lib.check(L.swb_project(cid, s["wd"].data_ptr(), h.data_ptr(), None, None, y.data_ptr(), H, shard,
+                                     0, sp))
+
+    ids = binding.config_ids()
+    if args.gate_config and args.down_config:
+        gcfg, dcfg, tuned = args.gate_config, args.down_config, None
+    else:
+        tuned = tune(torch, binding, launch_gate, launch_down, ids, stream)
+        gcfg = args.gate_config or tuned["gate"]
+        dcfg = args.down_config or tuned["down"]
+        if world > 1:  # every rank runs the same geometry: take rank 0's choice
+            t = torch.tensor([gcfg, dcfg], dtype=torch.int64, device=device)
+            dist.broadcast(t, 0)
+            gcfg, dcfg = int(t[0]), int(t[1])
+
+    def step(i):
+        launch_gate(gcfg, i)
+        launch_down(dcfg, i)
+        if world > 1:
+            dist.all_reduce(y)
+            _lib.check(L.swb_residual_epilogue(y.data_ptr(), bd.data_ptr(), x.data_ptr(), H, sp))
+
+    # ---- sanity check of the (sharded) layer against a plain torch fp32 computation
+    step(0)
+    torch.cuda.synchronize()
+    xf = x.float()
+    gref = w0["wg"].float() @ xf + common["bg"].float()
+    uref = w0["wu"].float() @ xf + common["bu"].float()
+    href = (torch.nn.functional.silu(gref) * uref).half()
+    yref = w0["wd"].float() @ href.float() + common["bd"].float() + xf
+    rel = ((y - yref).abs() / (yref.abs() + 1e-3 * yref.abs().max())).max().item()
+    del w0, gref, uref, href, yref
+    if not rel <= 2e-3:
+        raise SystemExit(f"bench sanity check failed on rank {rank}: max relative error {rel}")
+    launches_per_step = 2 if world == 1 else 3
+
+    # ---- CUDA graphs for the tensor-parallel step (launch overhead would dominate)
+    graphs = None
+    if world > 1:
+        graphs = []
+        for c in range(copies):
+            step(c)  # warm NCCL before capture
+        torch.cuda.synchronize()
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(c)
+            graphs.append(g)
+        torch.cuda.synchronize()
+
+    def run_step(i):
+        if graphs is None:
+            step(i)
+        else:
+            graphs[i % copies].replay()
+
+    sampler = ClockSampler(local).start()
+    for i in range(args.warmup):
+        run_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        run_step(i)
+    end.record(stream)
+    end.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    us_per_layer = elapsed_ms * 1e3 / args.steps
+
+    # ---- dominant kernel (gate): CUDA events around each launch, same rotating copies
+    gate_events = []
+    for i in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        launch_gate(gcfg, i)
+        b.record(stream)
+        launch_down(dcfg, i)
+        gate_events.append((a, b))
+    torch.cuda.synchronize()
+    gate_us = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in gate_events)
+    peaks = intensity.measured_peaks(ROOT / "MEASURED_PEAKS.json")
+    achieved = gate_bytes / (gate_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "kernel": f"gate (config {gcfg})", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                "peak_source": f"{peaks['source']} copy bandwidth",
+                "traffic": traffic_from_profile("gate", H, shard), "bytes_per_launch": gate_bytes,
+                "launch_us": gate_us}
+    layer_gbs = rank_bytes / (us_per_layer * 1e-6) / 1e9
+    layer_roofline = {"achieved": layer_gbs, "frac": layer_gbs / peaks["hbm_gbs"], "unit": "GB/s",
+                      "bytes_per_step_per_rank": rank_bytes}
+
+    # ---- all-reduce alone (tensor parallel): reported separately, it is latency-bound
+    tp = None
+    if world > 1:
+        ar = time_kernel(torch, lambda i: dist.all_reduce(y), 50, stream)
+        t = torch.tensor([ar], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tp = {"ranks": world, "shard_rows": shard, "allreduce_us": float(t.item()), "allreduce_bytes": H * 4,
+              "backend": "nccl"}
+
+    # ---- end to end through the public C-ABI call with host buffers (rank 0 path at N=1)
+    e2e = None
+    if world == 1:
+        x_host = common["x"].cpu().pin_memory()
+        y_host = torch.empty(H, dtype=torch.float32).pin_memory()
+        x_dev = torch.empty_like(x)
+        for i in range(3):
+            x_dev.copy_(x_host, non_blocking=True)
+            binding.ffn(x_dev, sets[i % copies]["wg"], sets[i % copies]["wu"], sets[i % copies]["wd"], bg, bu, bd, h, y,
+                        gcfg, dcfg, stream=sp)
+            y_host.copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(args.steps):
+            s = sets[i % copies]
+            x_dev.copy_(x_host, non_blocking=True)
+            binding.ffn(x_dev, s["wg"], s["wu"], s["wd"], bg, bu, bd, h, y, gcfg, dcfg, stream=sp)
+            y_host.copy_(y, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        e2e = {"value": a.elapsed_time(b) * 1e3 / args.steps, "unit": UNIT,
+               "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+               "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
+               "path": "swb_ffn via swiglu_b200.binding.ffn, pinned host x -> device -> pinned host y"}
+
+    # ---- cuBLAS GemmEx + pointwise on the same GPU (baseline, N=1)
+    cublas = None
+    if world == 1 and not args.no_cublas:
+        base = binding.CublasBaseline(device)
+        gbuf = torch.empty(I, dtype=torch.float32, device=device)
+        ubuf = torch.empty_like(gbuf)
+        hb = torch.empty(I, dtype=torch.float16, device=device)
+        yb = torch.empty(H, dtype=torch.float32, device=device)
+        res = {}
+        for algo in (0, 1):
+            fn = lambda i, a=algo: base.ffn(x, sets[i % copies]["wg"], sets[i % copies]["wu"],  # noqa: E731
+                                            sets[i % copies]["wd"], bg, bu, bd, gbuf, ubuf, hb, yb, algo=a, stream=sp)
+            for i in range(args.warmup):
+                fn(i)
+            res[algo] = time_kernel(torch, fn, args.steps, stream)
+        algo = min(res, key=res.get)
+        cublas = {"value": res[algo], "unit": UNIT, "algo": ["default", "default_tensor_op"][algo],
+                  "kernels_per_step": 5, "speedup_vs_cublas": res[algo] / us_per_layer}
+        base.close()
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(sets, common, H, I, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": us_per_layer, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
+                       "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
+                       "rotating_copies": copies,
+                       "l2": f"inputs larger than L2: {copies} rotating weight copies of "
+                             f"{weight_bytes_rank / 2**20:.0f} MiB per rank",
+                       "seed": 0, "weights": "N(0, 1/sqrt(K)) fp16", "x": "N(0,1)", "bias": "N(0,0.02)"},
+            "roofline": roofline, "layer_roofline": layer_roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "cublas_baseline": cublas, "tp": tp, "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
+            "gpu_name": torch.cuda.get_device_name(device),
+        }
+        if tuned is not None:
+            line["tuning_us"] = {"gate": {str(k): round(v, 3) for k, v in tuned["gate_times"].items()},
+                                 "down": {str(k): round(v, 3) for k, v in tuned["down_times"].items()}}
+        print(json.dumps(line), flush=True)
+
+    if graphs is not None:
+        del graphs
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,135 @@
+// Device helpers for sm_100a: streaming loads, bulk async copies, mbarriers
+// with bounded waits, fp16 unpacking and the SiLU activation.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace swb {
+
+// Upper bound for any wait on an mbarrier. A legitimate wait lasts at most the
+// latency of one bulk copy (microseconds); past this the kernel records
+// SWB_DEVERR_TIMEOUT in the device error word and stops instead of hanging.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Device error word of the translation unit that includes this header (one per
+// shared library); read and cleared by swb_device_error().
+static __device__ int g_device_error = 0;
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------- loads
+
+// 128-bit read-only streaming load: weights are read exactly once, so skip L1.
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_stream_b32(const void* p) {
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
+    __half2 h;
+    *reinterpret_cast<uint32_t*>(&h) = bits;
+    return __half22float2(h);
+}
+
+// ------------------------------------------------------------- mbarrier
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes initialised barriers visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase of `bar` with the given parity to complete. Gives up
+// after kWaitLimitNs, raising SWB_DEVERR_TIMEOUT, and returns false.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_device_error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ------------------------------------------------------- bulk async copy
+
+// L2 policy for data read exactly once (weights): evict first.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Global -> shared bulk copy completing on an mbarrier (non-multicast).
+// dst and src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+// Named barrier among the first `threads` threads of the CTA (id 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ----------------------------------------------------------- activation
+
+// SiLU(v) = v / (1 + exp(-v)), written in two branches so exp never overflows
+// (the same stable form as include/kernels.cuh:39-42 of the reference).
+__device__ __forceinline__ float silu(float v) {
+    if (v >= 0.f) return v / (1.f + expf(-v));
+    const float e = expf(v);
+    return v * e / (1.f + e);
+}
+
+__device__ __forceinline__ float round_half(float v) { return __half2float(__float2half_rn(v)); }
+
+}  // namespace swb

@@ -1,0 +1,416 @@
+// Batch-one projection kernels for sm_100a.
+//
+// One kernel body computes dot(W[row], x) for every row of a row-major fp16
+// matrix with fp32 accumulation, optionally a second matrix U against the same
+// x (the gated SwiGLU stage), and writes one of three epilogues:
+//   MODE_GATE: h = fp16(SiLU(a + bg) * (b + bu)), optionally with the eager
+//              fp16 rounding points (kernels.cuh:123-127 of the reference);
+//   MODE_F32 : y = a (+ bias) (+ residual), fp32;
+//   MODE_F16 : the same rounded to fp16.
+// These replace decode::project (include/kernels.cuh:24-114 of shubhxho/cuda-kernel).
+//
+// Two families:
+//   ldg_kernel  -- rows spread over CTAs, 128-bit (or 32-bit) streaming loads
+//                  with UNROLL loads per matrix in flight per thread, x staged
+//                  once per CTA in shared memory as fp32;
+//   bulk_kernel -- persistent: each CTA owns a balanced contiguous row range and
+//                  a producer thread streams it with cp.async.bulk into a ring
+//                  of shared-memory stages guarded by mbarriers; consumer warps
+//                  read each stage once. Row partial sums are combined in a
+//                  fixed order, so every configuration is deterministic.
+#pragma once
+
+#include <type_traits>
+
+#include "device.cuh"
+
+namespace swb {
+
+enum Mode : int { MODE_GATE = 0, MODE_F32 = 1, MODE_F16 = 2 };
+
+struct Params {
+    const __half* w;
+    const __half* u;
+    const __half* x;
+    const __half* bias;
+    const __half* ubias;
+    const __half* residual;
+    float* y;   // MODE_F32 output
+    __half* h;  // MODE_GATE / MODE_F16 output
+    int rows;
+    int cols;
+    int model_round;
+    int x_staged;  // ldg_kernel: x copied to shared memory as fp32
+    int stages;    // bulk_kernel: ring depth
+};
+
+template <int MODE>
+__device__ __forceinline__ void write_row(const Params& p, int row, float a, float b) {
+    if constexpr (MODE == MODE_GATE) {
+        if (p.bias) a += __half2float(p.bias[row]);
+        if (p.ubias) b += __half2float(p.ubias[row]);
+        if (p.model_round) {
+            a = round_half(a);
+            b = round_half(b);
+            const float s = round_half(silu(a));
+            p.h[row] = __float2half_rn(s * b);
+        } else {
+            p.h[row] = __float2half_rn(silu(a) * b);
+        }
+    } else {
+        if (p.bias) a += __half2float(p.bias[row]);
+        if (p.residual) a += __half2float(p.residual[row]);
+        if constexpr (MODE == MODE_F16)
+            p.h[row] = __float2half_rn(a);
+        else
+            p.y[row] = a;
+    }
+}
+
+// acc[k] += w(half2 k of the 8-half vector) . x[2k..2k+1]
+__device__ __forceinline__ void dot8(const uint4& wv, const float* xf, float* acc) {
+    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 wf = half2_bits_to_float2(words[k]);
+        acc[k] = fmaf(wf.x, xf[2 * k], acc[k]);
+        acc[k] = fmaf(wf.y, xf[2 * k + 1], acc[k]);
+    }
+}
+
+__device__ __forceinline__ float fold4(const float* acc) { return (acc[0] + acc[1]) + (acc[2] + acc[3]); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int d = 16; d; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    return v;
+}
+
+// x values for columns [c, c + PACK): from the fp32 shared copy when staged
+// (vector reads when 16/8-byte aligned), else from global fp16.
+template <int PACK>
+__device__ __forceinline__ void load_x(const Params& p, const float* xs, int c, bool xs_vec, float* xf) {
+    if (p.x_staged) {
+        if (xs_vec) {
+            if constexpr (PACK == 8) {
+                const float4 a = *reinterpret_cast<const float4*>(xs + c);
+                const float4 b = *reinterpret_cast<const float4*>(xs + c + 4);
+                xf[0] = a.x; xf[1] = a.y; xf[2] = a.z; xf[3] = a.w;
+                xf[4] = b.x; xf[5] = b.y; xf[6] = b.z; xf[7] = b.w;
+            } else {
+                const float2 a = *reinterpret_cast<const float2*>(xs + c);
+                xf[0] = a.x; xf[1] = a.y;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < PACK; ++i) xf[i] = xs[c + i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PACK; ++i) xf[i] = __half2float(p.x[c + i]);
+    }
+}
+
+__device__ __forceinline__ float load_x1(const Params& p, const float* xs, int c) {
+    return p.x_staged ? xs[c] : __half2float(p.x[c]);
+}
+
+// ======================================================================= LDG
+
+template <int WPR, int ROWS, int PACK, int UNROLL, int MODE>
+__global__ void __launch_bounds__(32 * WPR * ROWS) ldg_kernel(const Params p) {
+    static_assert(WPR > 0 && (WPR & (WPR - 1)) == 0 && ROWS > 0 && 32 * WPR * ROWS <= 1024, "geometry");
+    static_assert(PACK == 2 || PACK == 8, "pack");
+    constexpr bool GATED = MODE == MODE_GATE;
+    constexpr int NM = GATED ? 2 : 1;
+    constexpr int T = 32 * WPR;      // threads sharing one row
+    constexpr int VB = 2 * PACK;     // bytes per vector load
+    using Vec = typename std::conditional<PACK == 8, uint4, uint32_t>::type;
+
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float red[NM][ROWS * WPR];
+
+    const int cols = p.cols;
+    if (p.x_staged) {
+        for (int c = threadIdx.x; c < cols; c += blockDim.x) xs[c] = __half2float(p.x[c]);
+        __syncthreads();
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int group = warp / WPR, sub = warp % WPR;
+    const int t = sub * 32 + lane;
+    const int row = blockIdx.x * ROWS + group;
+
+    float acc[NM][4];
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[m][k] = 0.f;
+
+    if (row < p.rows) {
+        const __half* wr = p.w + size_t(row) * cols;
+        const __half* ur = GATED ? p.u + size_t(row) * cols : nullptr;
+        const uintptr_t wa = reinterpret_cast<uintptr_t>(wr);
+        bool vec = true;
+        if constexpr (GATED) vec = ((reinterpret_cast<uintptr_t>(ur) - wa) % VB) == 0;
+        // Scalar head up to the first VB-aligned weight, vector body, scalar tail.
+        int peel = vec ? int(((VB - wa % VB) % VB) / 2) : cols;
+        if (peel > cols) peel = cols;
+        const int nvec = (cols - peel) / PACK;
+        const int tail0 = peel + nvec * PACK;
+        const bool xs_vec = (peel % (PACK == 8 ? 4 : 2)) == 0;
+
+        for (int c = t; c < peel; c += T) {
+            const float xv = load_x1(p, xs, c);
+            acc[0][0] = fmaf(__half2float(wr[c]), xv, acc[0][0]);
+            if constexpr (GATED) acc[1][0] = fmaf(__half2float(ur[c]), xv, acc[1][0]);
+        }
+        const __half* wv0 = wr + peel;
+        const __half* uv0 = GATED ? ur + peel : nullptr;
+        int v = t;
+        for (; v + (UNROLL - 1) * T < nvec; v += UNROLL * T) {
+            Vec wv[UNROLL], uv[UNROLL];
+#pragma unroll
+            for (int i = 0; i < UNROLL; ++i) {
+                const size_t off = size_t(v + i * T) * PACK;
+                if constexpr (PACK == 8) {
+                    wv[i] = ldg_stream_v4(wv0 + off);
+                    if constexpr (GATED) uv[i] = ldg_stream_v4(uv0 + off);
+                } else {
+                    wv[i] = ldg_stream_b32(wv0 + off);
+                    if constexpr (GATED) uv[i] = ldg_stream_b32(uv0 + off);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < UNROLL; ++i) {
+                float xf[PACK];
+                load_x<PACK>(p, xs, peel + (v + i * T) * PACK, xs_vec, xf);
+                if constexpr (PACK == 8) {
+                    dot8(wv[i], xf, acc[0]);
+                    if constexpr (GATED) dot8(uv[i], xf, acc[1]);
+                } else {
+                    const int k = i & 3;
+                    const float2 wf = half2_bits_to_float2(wv[i]);
+                    acc[0][k] = fmaf(wf.y, xf[1], fmaf(wf.x, xf[0], acc[0][k]));
+                    if constexpr (GATED) {
+                        const float2 uf = half2_bits_to_float2(uv[i]);
+                        acc[1][k] = fmaf(uf.y, xf[1], fmaf(uf.x, xf[0], acc[1][k]));
+                    }
+                }
+            }
+        }
+        for (; v < nvec; v += T) {
+            const size_t off = size_t(v) * PACK;
+            float xf[PACK];
+            load_x<PACK>(p, xs, peel + v * PACK, xs_vec, xf);
+            if constexpr (PACK == 8) {
+                dot8(ldg_stream_v4(wv0 + off), xf, acc[0]);
+                if constexpr (GATED) dot8(ldg_stream_v4(uv0 + off), xf, acc[1]);
+            } else {
+                const float2 wf = half2_bits_to_float2(ldg_stream_b32(wv0 + off));
+                acc[0][0] = fmaf(wf.y, xf[1], fmaf(wf.x, xf[0], acc[0][0]));
+                if constexpr (GATED) {
+                    const float2 uf = half2_bits_to_float2(ldg_stream_b32(uv0 + off));
+                    acc[1][0] = fmaf(uf.y, xf[1], fmaf(uf.x, xf[0], acc[1][0]));
+                }
+            }
+        }
+        for (int c = tail0 + t; c < cols; c += T) {
+            const float xv = load_x1(p, xs, c);
+            acc[0][1] = fmaf(__half2float(wr[c]), xv, acc[0][1]);
+            if constexpr (GATED) acc[1][1] = fmaf(__half2float(ur[c]), xv, acc[1][1]);
+        }
+    }
+
+    float a = warp_sum(fold4(acc[0]));
+    float b = 0.f;
+    if constexpr (GATED) b = warp_sum(fold4(acc[1]));
+    if constexpr (WPR > 1) {
+        if (lane == 0) {
+            red[0][warp] = a;
+            if constexpr (GATED) red[NM - 1][warp] = b;
+        }
+        __syncthreads();
+        if (sub == 0 && lane == 0) {
+            a = 0.f;
+            b = 0.f;
+#pragma unroll
+            for (int j = 0; j < WPR; ++j) {
+                a += red[0][group * WPR + j];
+                if constexpr (GATED) b += red[NM - 1][group * WPR + j];
+            }
+        }
+    }
+    if (row < p.rows && sub == 0 && lane == 0) write_row<MODE>(p, row, a, b);
+}
+
+// ====================================================================== BULK
+
+// Shared-memory layout of bulk_kernel, shared by host sizing and device code.
+struct BulkLayout {
+    size_t ring, full, empty, xs, part, total;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline BulkLayout bulk_layout(int nm, int chunk, int stages, int cols, int cw,
+                                                  int rows_per_cta) {
+    BulkLayout L;
+    L.ring = 0;
+    size_t off = size_t(stages) * nm * chunk * 2;
+    L.full = align_up(off, 16);
+    L.empty = L.full + size_t(stages) * 8;
+    L.xs = align_up(L.empty + size_t(stages) * 8, 16);
+    L.part = align_up(L.xs + size_t(cols) * 4, 16);
+    L.total = align_up(L.part + size_t(rows_per_cta) * cw * nm * 4, 16);
+    return L;
+}
+
+template <int CW, int CHUNK, int MODE>
+__global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) {
+    static_assert(CHUNK % 8 == 0 && CHUNK > 0, "chunk must be whole 16-byte vectors");
+    constexpr bool GATED = MODE == MODE_GATE;
+    constexpr int NM = GATED ? 2 : 1;
+    constexpr int CT = CW * 32;  // consumer threads
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int s_failed;
+
+    const int G = gridDim.x;
+    const int r0 = int((long long)blockIdx.x * p.rows / G);
+    const int r1 = int((long long)(blockIdx.x + 1) * p.rows / G);
+    const int nrows = r1 - r0;
+    if (nrows <= 0) return;  // whole CTA leaves together
+    const int cols = p.cols;
+    const int stages = p.stages;
+    const int nch = (cols + CHUNK - 1) / CHUNK;
+    const int units = nrows * nch;
+    const int rows_per_cta = (p.rows + G - 1) / G;
+
+    const BulkLayout L = bulk_layout(NM, CHUNK, stages, cols, CW, rows_per_cta);
+    __half* ring = reinterpret_cast<__half*>(smem + L.ring);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    float* xs = reinterpret_cast<float*>(smem + L.xs);
+    float* part = reinterpret_cast<float*>(smem + L.part);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        s_failed = 0;
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), CW);
+        }
+        mbar_fence_init();
+    }
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) xs[c] = __half2float(p.x[c]);
+    __syncthreads();
+
+    if (warp == CW) {
+        // ------------------------------------------------------- producer
+        if (lane != 0) return;
+        const uint64_t pol = l2_evict_first_policy();
+        int s = 0, row = r0, ch = 0, issued = 0;
+        uint32_t ph = 0;
+        for (int k = 0; k < units; ++k) {
+            if (k >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) break;
+            const int c0 = ch * CHUNK;
+            const int len = min(CHUNK, cols - c0);
+            const uint32_t bytes = uint32_t(len) * 2u;
+            const uint32_t fb = smem_u32(full + s);
+            mbar_arrive_expect_tx(fb, bytes * NM);
+            const size_t goff = size_t(row) * cols + c0;
+            bulk_copy_g2s(smem_u32(ring + size_t(s) * NM * CHUNK), p.w + goff, bytes, fb, pol);
+            if constexpr (GATED) bulk_copy_g2s(smem_u32(ring + (size_t(s) * NM + 1) * CHUNK), p.u + goff, bytes, fb, pol);
+            ++issued;
+            if (++ch == nch) { ch = 0; ++row; }
+            if (++s == stages) { s = 0; ph ^= 1u; }
+        }
+        // Never leave with copies in flight: wait (bounded) for the last fills.
+        const int drain = issued < stages ? issued : stages;
+        for (int j = 1; j <= drain; ++j) {
+            const int k = issued - j;
+            if (!mbar_wait(smem_u32(full + (k % stages)), uint32_t((k / stages) & 1))) break;
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    const int t = threadIdx.x;
+    float acc[NM][4];
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[m][k] = 0.f;
+
+    int s = 0, row = r0, ch = 0;
+    uint32_t ph = 0;
+    for (int k = 0; k < units; ++k) {
+        if (!mbar_wait(smem_u32(full + s), ph)) {
+            s_failed = 1;
+            break;
+        }
+        const int c0 = ch * CHUNK;
+        const int nv = min(CHUNK, cols - c0) / 8;
+        const __half* sw = ring + size_t(s) * NM * CHUNK;
+        for (int v = t; v < nv; v += CT) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(sw + v * 8);
+            const float4 xa = *reinterpret_cast<const float4*>(xs + c0 + v * 8);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + c0 + v * 8 + 4);
+            const float xf[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            dot8(wv, xf, acc[0]);
+            if constexpr (GATED) {
+                const uint4 uv = *reinterpret_cast<const uint4*>(sw + CHUNK + v * 8);
+                dot8(uv, xf, acc[1]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        if (++ch == nch) {
+            const float a = warp_sum(fold4(acc[0]));
+            float b = 0.f;
+            if constexpr (GATED) b = warp_sum(fold4(acc[1]));
+            if (lane == 0) {
+                part[(size_t(row - r0) * CW + warp) * NM] = a;
+                if constexpr (GATED) part[(size_t(row - r0) * CW + warp) * NM + 1] = b;
+            }
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
+            ch = 0;
+            ++row;
+        }
+        if (++s == stages) { s = 0; ph ^= 1u; }
+    }
+    named_barrier_sync(1, CT);
+    if (s_failed) return;
+    for (int i = t; i < nrows; i += CT) {
+        float a = 0.f, b = 0.f;
+        for (int j = 0; j < CW; ++j) {
+            a += part[(size_t(i) * CW + j) * NM];
+            if constexpr (GATED) b += part[(size_t(i) * CW + j) * NM + 1];
+        }
+        write_row<MODE>(p, r0 + i, a, b);
+    }
+}
+
+// ============================================================== pointwise
+
+// kernels.cuh:155-162 of the reference: the cuBLAS path's gate epilogue.
+__global__ void gate_epilogue_kernel(const float* a, const float* b, const __half* bg, const __half* bu,
+                                     __half* h, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const float g = a[i] + __half2float(bg[i]);
+        const float v = b[i] + __half2float(bu[i]);
+        h[i] = __float2half_rn(silu(g) * v);
+    }
+}
+
+// kernels.cuh:163-166 of the reference: y += bias + x.
+__global__ void residual_epilogue_kernel(float* y, const __half* bias, const __half* x, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] += __half2float(bias[i]) + __half2float(x[i]);
+}
+
+}  // namespace swb

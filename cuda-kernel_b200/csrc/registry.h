@@ -1,0 +1,50 @@
+// One list of launch geometries generates both the host metadata
+// (swb_config_ids / swb_config_info) and the CUDA dispatch switch, the way
+// DECODE_CONFIGS does in include/config.hpp:7-11 of shubhxho/cuda-kernel.
+//
+// X(id, family, warps, rows, pack, unroll, chunk, stages)
+//
+// LDG family (register streaming; x staged in shared memory as fp32):
+//   warps  = warps per output row, rows = output rows per CTA,
+//   pack   = halves per vector load (2 -> 32-bit, 8 -> 128-bit),
+//   unroll = independent vector loads per matrix kept in flight per thread.
+//   Ids 1..21 keep the reference's (id, warps, rows, pack) geometries so tuned
+//   ids from the reference stay valid; ids 32+ are deep-unrolled B200 variants.
+// BULK family (persistent, one CTA set per SM):
+//   warps  = consumer warps (plus one producer warp), rows = CTAs per SM,
+//   chunk  = halves per matrix per ring stage, stages = maximum ring depth
+//   (the launcher trims it to the shared memory the shape leaves free).
+//   A BULK id whose preconditions fail for a shape (cols % 8, 16-byte rows,
+//   shared-memory fit) runs the LDG geometry of id 33 instead.
+#pragma once
+
+#define SWB_FAM_LDG 0
+#define SWB_FAM_BULK 1
+
+#define SWB_CONFIGS(X)                                                                          \
+    X(1, SWB_FAM_LDG, 1, 4, 2, 1, 0, 0)                                                         \
+    X(2, SWB_FAM_LDG, 2, 4, 2, 1, 0, 0)                                                         \
+    X(4, SWB_FAM_LDG, 4, 4, 2, 1, 0, 0)                                                         \
+    X(8, SWB_FAM_LDG, 8, 4, 2, 1, 0, 0)                                                         \
+    X(16, SWB_FAM_LDG, 1, 4, 8, 1, 0, 0)                                                        \
+    X(17, SWB_FAM_LDG, 2, 4, 8, 1, 0, 0)                                                        \
+    X(18, SWB_FAM_LDG, 4, 2, 8, 1, 0, 0)                                                        \
+    X(19, SWB_FAM_LDG, 1, 8, 8, 1, 0, 0)                                                        \
+    X(20, SWB_FAM_LDG, 2, 2, 8, 1, 0, 0)                                                        \
+    X(21, SWB_FAM_LDG, 4, 1, 8, 1, 0, 0)                                                        \
+    X(32, SWB_FAM_LDG, 1, 8, 8, 4, 0, 0)                                                        \
+    X(33, SWB_FAM_LDG, 2, 4, 8, 4, 0, 0)                                                        \
+    X(34, SWB_FAM_LDG, 4, 2, 8, 4, 0, 0)                                                        \
+    X(35, SWB_FAM_LDG, 8, 1, 8, 4, 0, 0)                                                        \
+    X(36, SWB_FAM_LDG, 1, 4, 8, 8, 0, 0)                                                        \
+    X(37, SWB_FAM_LDG, 2, 2, 8, 8, 0, 0)                                                        \
+    X(38, SWB_FAM_LDG, 4, 1, 8, 8, 0, 0)                                                        \
+    X(64, SWB_FAM_BULK, 8, 1, 8, 1, 4096, 8)                                                    \
+    X(65, SWB_FAM_BULK, 8, 1, 8, 1, 2048, 16)                                                   \
+    X(66, SWB_FAM_BULK, 4, 1, 8, 1, 4096, 8)                                                    \
+    X(67, SWB_FAM_BULK, 16, 1, 8, 1, 8192, 4)                                                   \
+    X(68, SWB_FAM_BULK, 8, 2, 8, 1, 2048, 8)                                                    \
+    X(69, SWB_FAM_BULK, 4, 2, 8, 1, 4096, 4)
+
+// Id used when a BULK geometry cannot run a shape.
+#define SWB_BULK_FALLBACK_ID 33

@@ -1,0 +1,343 @@
+// C ABI of the B200 SwiGLU decode layer (declarations: include/swiglu_b200.h).
+//
+// Argument guards mirror decode::launch (include/kernels.cuh:136-154) and the
+// torch binding (src/torch_extension.cu:7-40) of shubhxho/cuda-kernel, in the
+// same order and with the same messages, and run before any CUDA call.
+// Dispatch is generated from the registry list (registry.h), as
+// include/kernels.cuh:145-153 generates it from DECODE_CONFIGS.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <string>
+
+#include "kernels.cuh"
+#include "registry.h"
+#include "swiglu_b200.h"
+
+namespace swb {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* detail = nullptr) {
+    g_last_error = swb_status_string(status);
+    if (detail && *detail) {
+        g_last_error += ": ";
+        g_last_error += detail;
+    }
+    return status;
+}
+
+int check_launch() {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    return SWB_OK;
+}
+
+constexpr swb_config_t kConfigs[] = {
+#define SWB_META(ID, FAM, W, R, PK, U, CH, ST) {ID, FAM, W, R, PK, U, CH, ST},
+    SWB_CONFIGS(SWB_META)
+#undef SWB_META
+};
+constexpr int kConfigCount = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
+
+const swb_config_t* find_config(int64_t id) {
+    for (const auto& c : kConfigs)
+        if (c.id == id) return &c;
+    return nullptr;
+}
+
+// Geometry invariants checked at compile time for every registry entry.
+#define SWB_CHECK(ID, FAM, W, R, PK, U, CH, ST)                                                     \
+    static_assert(ID > 0 && ID < 1000, "ids 0 and >= 1000 stay invalid");                          \
+    static_assert(FAM != SWB_FAM_LDG || (32 * W * R <= 1024 && (W & (W - 1)) == 0), "LDG block");   \
+    static_assert(FAM != SWB_FAM_LDG || PK == 2 || PK == 8, "LDG pack");                            \
+    static_assert(FAM != SWB_FAM_LDG || U == 1 || U == 2 || U == 4 || U == 8, "LDG unroll");        \
+    static_assert(FAM != SWB_FAM_BULK || (CH % 8 == 0 && CH > 0 && ST >= 2 && (W + 1) * 32 <= 1024), \
+                  "BULK geometry");
+SWB_CONFIGS(SWB_CHECK)
+#undef SWB_CHECK
+
+// Shared-memory capacities of sm_100: 228 KB per SM, 227 KB opt-in per CTA,
+// 1 KB reserved per resident CTA.
+constexpr size_t kSmemPerSm = 233472;
+constexpr size_t kSmemPerCtaMax = 232448;
+// x is staged in shared memory by the LDG family while its fp32 copy fits this.
+constexpr size_t kXStageLimit = 96 * 1024;
+
+int sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    if (dev < 64) {
+        const int c = cache[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device.
+template <typename Kernel>
+int ensure_smem(Kernel kernel, std::atomic<uint64_t>& done_mask, size_t bytes) {
+    if (bytes <= 48 * 1024) return SWB_OK;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch();
+    const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+    if (bit && (done_mask.load(std::memory_order_acquire) & bit)) return SWB_OK;
+    // Static shared memory counts against the same 227 KB per-CTA limit.
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    if (bytes + fa.sharedSizeBytes > kSmemPerCtaMax) return fail(SWB_E_CUDA, "shared memory request too large");
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(kSmemPerCtaMax - fa.sharedSizeBytes));
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    if (bit) done_mask.fetch_or(bit, std::memory_order_acq_rel);
+    return SWB_OK;
+}
+
+template <int W, int R, int PK, int U, int MODE>
+int launch_ldg(Params p, cudaStream_t stream) {
+    static std::atomic<uint64_t> smem_set{0};
+    p.x_staged = size_t(p.cols) * 4 <= kXStageLimit;
+    const size_t smem = p.x_staged ? align_up(size_t(p.cols) * 4, 16) : 0;
+    auto kernel = ldg_kernel<W, R, PK, U, MODE>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    const unsigned grid = unsigned((p.rows + R - 1) / R);
+    kernel<<<grid, 32 * W * R, smem, stream>>>(p);
+    return check_launch();
+}
+
+template <int CW, int CPS, int CH, int ST, int MODE>
+int launch_bulk(Params p, cudaStream_t stream);
+
+template <int MODE>
+int run_fallback(Params p, cudaStream_t stream);
+
+template <int FAM, int W, int R, int PK, int U, int CH, int ST>
+struct Launcher;
+
+template <int W, int R, int PK, int U, int CH, int ST>
+struct Launcher<SWB_FAM_LDG, W, R, PK, U, CH, ST> {
+    template <int MODE>
+    static int run(Params p, cudaStream_t s) {
+        return launch_ldg<W, R, PK, U, MODE>(p, s);
+    }
+};
+
+template <int W, int R, int PK, int U, int CH, int ST>
+struct Launcher<SWB_FAM_BULK, W, R, PK, U, CH, ST> {
+    template <int MODE>
+    static int run(Params p, cudaStream_t s) {
+        return launch_bulk<W, R, CH, ST, MODE>(p, s);
+    }
+};
+
+template <int CW, int CPS, int CH, int ST, int MODE>
+int launch_bulk(Params p, cudaStream_t stream) {
+    constexpr int NM = MODE == MODE_GATE ? 2 : 1;
+    static std::atomic<uint64_t> smem_set{0};
+    const bool aligned = (p.cols % 8) == 0 && (reinterpret_cast<uintptr_t>(p.w) % 16) == 0 &&
+                         (NM == 1 || (reinterpret_cast<uintptr_t>(p.u) % 16) == 0);
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const int G = std::min(sms * CPS, p.rows);
+    const int rows_per_cta = (p.rows + G - 1) / G;
+    const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 64;
+    int stages = ST;
+    while (stages >= 2 && bulk_layout(NM, CH, stages, p.cols, CW, rows_per_cta).total > budget) --stages;
+    if (!aligned || stages < 2) return run_fallback<MODE>(p, stream);
+    p.stages = stages;
+    p.x_staged = 1;
+    const size_t smem = bulk_layout(NM, CH, stages, p.cols, CW, rows_per_cta).total;
+    auto kernel = bulk_kernel<CW, CH, MODE>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    kernel<<<unsigned(G), (CW + 1) * 32, smem, stream>>>(p);
+    return check_launch();
+}
+
+template <int MODE>
+int dispatch(int64_t id, const Params& p, cudaStream_t s) {
+    switch (id) {
+#define SWB_CASE(ID, FAM, W, R, PK, U, CH, ST) \
+    case ID:                                   \
+        return Launcher<FAM, W, R, PK, U, CH, ST>::template run<MODE>(p, s);
+        SWB_CONFIGS(SWB_CASE)
+#undef SWB_CASE
+        default:
+            return fail(SWB_E_CONFIG);
+    }
+}
+
+template <int MODE>
+int run_fallback(Params p, cudaStream_t stream) {
+    return dispatch<MODE>(SWB_BULK_FALLBACK_ID, p, stream);
+}
+
+bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {
+    const uintptr_t ap = reinterpret_cast<uintptr_t>(a), bp = reinterpret_cast<uintptr_t>(b);
+    return ap < bp + bbytes && bp < ap + abytes;
+}
+
+Params make_params() {
+    Params p;
+    std::memset(&p, 0, sizeof p);
+    return p;
+}
+
+}  // namespace
+}  // namespace swb
+
+using namespace swb;
+
+extern "C" {
+
+const char* swb_status_string(int status) {
+    switch (status) {
+        case SWB_OK: return "ok";
+        case SWB_E_INPUT: return "invalid projection input";
+        case SWB_E_GATE_BUFFERS: return "invalid gate buffers";
+        case SWB_E_HALF_OUTPUT: return "missing half output";
+        case SWB_E_FLOAT_OUTPUT: return "missing float output";
+        case SWB_E_RESIDUAL: return "missing residual";
+        case SWB_E_CONFIG: return "unknown kernel configuration";
+        case SWB_E_SHAPE: return "invalid shape";
+        case SWB_E_CONFIG_RANGE: return "configuration out of range";
+        case SWB_E_CONFIG_INVALID: return "invalid configuration";
+        case SWB_E_OVERLAP_INPUT: return "workspace overlaps input storage";
+        case SWB_E_OVERLAP_OUTPUT: return "scratch and output overlap";
+        case SWB_E_CUDA: return "CUDA error";
+        case SWB_E_DEVICE: return "device-side error";
+        case SWB_E_UNSUPPORTED: return "unsupported device";
+        default: return "unknown status";
+    }
+}
+
+const char* swb_last_error(void) { return g_last_error.c_str(); }
+
+int swb_version(void) { return 1; }
+
+int swb_config_count(void) { return kConfigCount; }
+
+int swb_config_ids(int* out, int cap) {
+    if (out)
+        for (int i = 0; i < kConfigCount && i < cap; ++i) out[i] = kConfigs[i].id;
+    return kConfigCount;
+}
+
+int swb_valid_config(int64_t id) { return find_config(id) != nullptr; }
+
+int swb_config_info(int64_t id, swb_config_t* out) {
+    const swb_config_t* c = find_config(id);
+    if (!c) return fail(SWB_E_CONFIG);
+    if (out) *out = *c;
+    return SWB_OK;
+}
+
+int swb_gate(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu, void* h,
+             int rows, int cols, int model_round, void* stream) {
+    if (rows <= 0 || cols <= 0 || !wg || !x) return fail(SWB_E_INPUT);
+    if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
+    if (!find_config(config)) return fail(SWB_E_CONFIG);
+    Params p = make_params();
+    p.w = static_cast<const __half*>(wg);
+    p.u = static_cast<const __half*>(wu);
+    p.x = static_cast<const __half*>(x);
+    p.bias = static_cast<const __half*>(bg);
+    p.ubias = static_cast<const __half*>(bu);
+    p.h = static_cast<__half*>(h);
+    p.rows = rows;
+    p.cols = cols;
+    p.model_round = model_round ? 1 : 0;
+    return dispatch<MODE_GATE>(config, p, static_cast<cudaStream_t>(stream));
+}
+
+int swb_project(int config, const void* w, const void* x, const void* bias, const void* residual, void* out,
+                int rows, int cols, unsigned flags, void* stream) {
+    if (rows <= 0 || cols <= 0 || !w || !x) return fail(SWB_E_INPUT);
+    const bool half_out = (flags & SWB_HALF_OUT) != 0;
+    if (!out) return fail(half_out ? SWB_E_HALF_OUTPUT : SWB_E_FLOAT_OUTPUT);
+    if ((flags & SWB_RESIDUAL) && !residual) return fail(SWB_E_RESIDUAL);
+    if (!find_config(config)) return fail(SWB_E_CONFIG);
+    Params p = make_params();
+    p.w = static_cast<const __half*>(w);
+    p.x = static_cast<const __half*>(x);
+    p.bias = static_cast<const __half*>(bias);
+    p.residual = (flags & SWB_RESIDUAL) ? static_cast<const __half*>(residual) : nullptr;
+    p.rows = rows;
+    p.cols = cols;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (half_out) {
+        p.h = static_cast<__half*>(out);
+        return dispatch<MODE_F16>(config, p, s);
+    }
+    p.y = static_cast<float*>(out);
+    return dispatch<MODE_F32>(config, p, s);
+}
+
+int swb_ffn(int gate_config, int down_config, const void* wg, const void* wu, const void* wd, const void* x,
+            const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
+            void* stream) {
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
+    if (!wd) return fail(SWB_E_INPUT);
+    if (!y) return fail(SWB_E_FLOAT_OUTPUT);
+    if (int rc = swb_gate(gate_config, wg, wu, x, bg, bu, h, inter, hidden, 0, stream)) return rc;
+    return swb_project(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream);
+}
+
+int swb_swiglu_out(const void* x, const void* gate, const void* up, const void* down, void* h, void* y,
+                   int64_t hidden, int64_t intermediate, int64_t gate_config, int64_t down_config, void* stream) {
+    if (!(hidden > 0 && intermediate > 0 && hidden <= 100000 && intermediate <= 100000)) return fail(SWB_E_SHAPE);
+    if (!(gate_config >= 0 && gate_config <= 1000 && down_config >= 0 && down_config <= 1000))
+        return fail(SWB_E_CONFIG_RANGE);
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG_INVALID);
+    if (!x || !gate || !down) return fail(SWB_E_INPUT);
+    if (!up || !h) return fail(SWB_E_GATE_BUFFERS);
+    if (!y) return fail(SWB_E_HALF_OUTPUT);
+    const size_t hb = size_t(hidden) * 2, ib = size_t(intermediate) * 2, wb = size_t(hidden) * size_t(intermediate) * 2;
+    const void* inputs[4] = {x, gate, up, down};
+    const size_t sizes[4] = {hb, wb, wb, wb};
+    for (int i = 0; i < 4; ++i)
+        if (overlaps(h, ib, inputs[i], sizes[i]) || overlaps(y, hb, inputs[i], sizes[i]))
+            return fail(SWB_E_OVERLAP_INPUT);
+    if (overlaps(h, ib, y, hb)) return fail(SWB_E_OVERLAP_OUTPUT);
+    if (int rc = swb_gate(int(gate_config), gate, up, x, nullptr, nullptr, h, int(intermediate), int(hidden), 1, stream))
+        return rc;
+    return swb_project(int(down_config), down, h, nullptr, nullptr, y, int(hidden), int(intermediate), SWB_HALF_OUT,
+                       stream);
+}
+
+int swb_gate_epilogue(const float* a, const float* b, const void* bg, const void* bu, void* h, int n, void* stream) {
+    if (n <= 0 || !a || !b || !bg || !bu || !h) return fail(SWB_E_INPUT);
+    gate_epilogue_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        a, b, static_cast<const __half*>(bg), static_cast<const __half*>(bu), static_cast<__half*>(h), n);
+    return check_launch();
+}
+
+int swb_residual_epilogue(float* y, const void* bias, const void* x, int n, void* stream) {
+    if (n <= 0 || !y || !bias || !x) return fail(SWB_E_INPUT);
+    residual_epilogue_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        y, static_cast<const __half*>(bias), static_cast<const __half*>(x), n);
+    return check_launch();
+}
+
+int swb_device_error(int clear, int* out) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof v);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    if (clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero);
+        if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    }
+    if (out) *out = v;
+    return SWB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,126 @@
+/*
+ * swiglu_b200 -- C ABI of the B200 (sm_100a) batch-one SwiGLU decode layer.
+ *
+ *   gate = Wg x + bg,  up = Wu x + bu,  h = SiLU(gate) * up,  y = Wd h + bd + x
+ *
+ * fp16 weights/inputs, fp32 accumulation, fp16 h, fp32 (or fp16) y. Every entry
+ * point takes plain device pointers and sizes, launches asynchronously on the
+ * given stream (a cudaStream_t, NULL = legacy default stream) on the CURRENT
+ * device, allocates nothing, and returns 0 or a SWB_E_* status. Argument checks
+ * run before any CUDA call, so invalid calls fail without touching a GPU.
+ *
+ * Each declaration names the interface of shubhxho/cuda-kernel it replaces.
+ * Library: cuda-kernel_b200/lib/libswiglu_b200.so (cudart linked statically).
+ */
+#ifndef SWIGLU_B200_H
+#define SWIGLU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef SWB_API
+#define SWB_API __attribute__((visibility("default")))
+#endif
+
+/* ---- status codes; swb_status_string() gives the reference's message ---- */
+#define SWB_OK 0
+#define SWB_E_INPUT 1          /* "invalid projection input"      include/kernels.cuh:140 */
+#define SWB_E_GATE_BUFFERS 2   /* "invalid gate buffers"          include/kernels.cuh:141 */
+#define SWB_E_HALF_OUTPUT 3    /* "missing half output"           include/kernels.cuh:142 */
+#define SWB_E_FLOAT_OUTPUT 4   /* "missing float output"          include/kernels.cuh:143 */
+#define SWB_E_RESIDUAL 5       /* "missing residual"              include/kernels.cuh:144 */
+#define SWB_E_CONFIG 6         /* "unknown kernel configuration"  include/kernels.cuh:151, config.hpp:19 */
+#define SWB_E_SHAPE 7          /* "invalid shape"                 src/torch_extension.cu:17 */
+#define SWB_E_CONFIG_RANGE 8   /* "configuration out of range"    src/torch_extension.cu:21 */
+#define SWB_E_CONFIG_INVALID 9 /* "invalid configuration"         src/torch_extension.cu:22 */
+#define SWB_E_OVERLAP_INPUT 10 /* "workspace overlaps input storage" src/torch_extension.cu:27-29 */
+#define SWB_E_OVERLAP_OUTPUT 11 /* "scratch and output overlap"   src/torch_extension.cu:30 */
+#define SWB_E_CUDA 12          /* CUDA runtime error; detail in swb_last_error() */
+#define SWB_E_DEVICE 13        /* a kernel gave up a bounded wait (device error word set) */
+#define SWB_E_UNSUPPORTED 14   /* no usable sm_100 device / feature */
+
+/* project() flags (template flags of decode::launch, include/kernels.cuh:136) */
+#define SWB_RESIDUAL 1u /* add residual[row] after bias (RESIDUAL) */
+#define SWB_HALF_OUT 2u /* write fp16 into out instead of fp32 (HALF_OUT) */
+
+/* kernel families in the registry */
+#define SWB_FAMILY_LDG 0  /* register-streaming 128/32-bit loads, x staged in shared memory */
+#define SWB_FAMILY_BULK 1 /* persistent: cp.async.bulk ring + mbarriers, one producer warp */
+
+/* Host metadata of one launch geometry (include/config.hpp:5 struct Config). */
+typedef struct swb_config {
+    int id;
+    int family;  /* SWB_FAMILY_* */
+    int warps;   /* LDG: warps per output row. BULK: consumer warps per CTA */
+    int rows;    /* LDG: rows per CTA. BULK: CTAs per SM */
+    int pack;    /* halves per vector load (2 = 32-bit, 8 = 128-bit) */
+    int unroll;  /* LDG: independent vector loads in flight per matrix per thread */
+    int chunk;   /* BULK: halves per matrix per pipeline stage (0 for LDG) */
+    int stages;  /* BULK: maximum ring depth (0 for LDG) */
+} swb_config_t;
+
+SWB_API const char* swb_status_string(int status);
+/* Detail of the last failing call on the calling host thread ("" if none). */
+SWB_API const char* swb_last_error(void);
+SWB_API int swb_version(void);
+
+/* ---- registry: replaces include/config.hpp:7-20 and torch_extension.cu:52 config_ids() ---- */
+SWB_API int swb_config_count(void);
+/* Writes up to cap ids in registry order; returns the total count. */
+SWB_API int swb_config_ids(int* out, int cap);
+/* config.hpp:13-16 valid_config(id); takes int64 so callers need not narrow first. */
+SWB_API int swb_valid_config(int64_t id);
+/* config.hpp:17-20 config(id); SWB_E_CONFIG for unknown ids. */
+SWB_API int swb_config_info(int64_t id, swb_config_t* out);
+
+/* ---- kernels: replace decode::launch<GATED,RESIDUAL,HALF_OUT,MODEL_ROUND>, kernels.cuh:136-154 ---- */
+
+/* launch<true,false,false,MODEL_ROUND>: h[i] = fp16(SiLU(Wg[i].x + bg[i]) * (Wu[i].x + bu[i])).
+ * Wg, Wu: [rows, cols] row-major fp16; x: [cols]; bg, bu: [rows] or NULL; h: [rows] fp16.
+ * model_round != 0 rounds to fp16 after each dot, after SiLU and after the product
+ * (kernels.cuh:123-127), matching eager fp16 Linear -> SiLU -> multiply. */
+SWB_API int swb_gate(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu,
+             void* h, int rows, int cols, int model_round, void* stream);
+
+/* launch<false,RESIDUAL,HALF_OUT>: out[r] = W[r].x (+ bias[r]) (+ residual[r]).
+ * W: [rows, cols]; x: [cols]; bias: [rows] or NULL; residual: [rows] (required with SWB_RESIDUAL).
+ * out: float[rows], or fp16[rows] with SWB_HALF_OUT. */
+SWB_API int swb_project(int config, const void* w, const void* x, const void* bias, const void* residual, void* out,
+                int rows, int cols, unsigned flags, void* stream);
+
+/* Workload::custom(ffn=true), src/benchmark.cu:161-165: the whole layer with biases
+ * and residual. h: [inter] fp16 workspace (overwritten); y: [hidden] fp32. */
+SWB_API int swb_ffn(int gate_config, int down_config, const void* wg, const void* wu, const void* wd, const void* x,
+            const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
+            void* stream);
+
+/* swiglu_out, src/torch_extension.cu:7-40: the binding's shape / config / alias guards,
+ * then the model-rounding gate into h [inter] and the fp16 down projection into
+ * y [hidden] (no bias, no residual -- the residual stays in the transformer layer).
+ * gate, up: [inter, hidden]; down: [hidden, inter]. Ids are checked against
+ * [0, 1000] before narrowing, as the binding does. */
+SWB_API int swb_swiglu_out(const void* x, const void* gate, const void* up, const void* down, void* h, void* y,
+                   int64_t hidden, int64_t intermediate, int64_t gate_config, int64_t down_config,
+                   void* stream);
+
+/* ---- pointwise kernels of the cuBLAS path: kernels.cuh:155-166 ---- */
+/* gate_epilogue: h[i] = fp16(SiLU(a[i] + bg[i]) * (b[i] + bu[i])) */
+SWB_API int swb_gate_epilogue(const float* a, const float* b, const void* bg, const void* bu, void* h, int n,
+                      void* stream);
+/* residual_epilogue: y[i] += bias[i] + x[i]; also closes a tensor-parallel layer
+ * after the all-reduce of the partial y. */
+SWB_API int swb_residual_epilogue(float* y, const void* bias, const void* x, int n, void* stream);
+
+/* Device error word of the current device: OR of SWB_DEVERR_* raised by kernels
+ * whose bounded waits expired. Synchronises the device. clear != 0 resets it. */
+#define SWB_DEVERR_TIMEOUT 1
+SWB_API int swb_device_error(int clear, int* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SWIGLU_B200_H */

@@ -1,0 +1,151 @@
+"""C ABI checks that need no GPU: exports, registry metadata, argument guards.
+
+Every guard in swiglu_b200.h runs before any CUDA call, so invalid calls are
+exercised here with fake pointers; nothing is launched.
+"""
+import ctypes
+import subprocess
+
+import pytest
+
+from swiglu_b200 import _lib
+
+FAKE = 0x7F0000000000  # never dereferenced: every call below fails a guard first
+
+
+def L():
+    return _lib.lib()
+
+
+def test_library_exports_every_declared_symbol():
+    declared = _lib.declared_symbols()
+    api_lines = sum(h.read_text().count("\nSWB_API ") for h in _lib.HEADERS)
+    assert len(declared) == api_lines >= 19
+    for path in (_lib.LIB_PATH, _lib.CUBLAS_LIB_PATH):
+        out = subprocess.run(["nm", "-D", "--defined-only", str(path)], capture_output=True, text=True, check=True)
+        exported = {line.split()[-1] for line in out.stdout.splitlines() if " T " in line}
+        mine = [s for s in declared if (s.startswith("swbl_") == (path == _lib.CUBLAS_LIB_PATH))]
+        missing = [s for s in mine if s not in exported]
+        assert not missing, (path.name, missing)
+        # nothing but the declared C ABI leaks out of the product library
+        assert exported <= set(declared), exported - set(declared)
+    for s in declared:
+        assert hasattr(_lib.cublas_lib() if s.startswith("swbl_") else L(), s)
+
+
+def test_library_is_sm100a_only_and_self_contained():
+    out = subprocess.run(["ldd", str(_lib.LIB_PATH)], capture_output=True, text=True, check=True).stdout
+    assert "libcudart" not in out  # runtime linked statically: nothing to resolve on the box
+    assert "libcublas" not in out  # the product path does not depend on cuBLAS
+
+
+def test_status_strings_match_reference_messages():
+    expected = {
+        1: "invalid projection input", 2: "invalid gate buffers", 3: "missing half output",
+        4: "missing float output", 5: "missing residual", 6: "unknown kernel configuration",
+        7: "invalid shape", 8: "configuration out of range", 9: "invalid configuration",
+        10: "workspace overlaps input storage", 11: "scratch and output overlap",
+    }
+    for code, msg in expected.items():
+        assert _lib.status_message(code) == msg
+
+
+def test_registry_keeps_reference_ids_and_rejects_invalid():
+    from swiglu_b200 import config_ids, valid_config, config_info
+    ids = config_ids()
+    assert ids[:10] == [1, 2, 4, 8, 16, 17, 18, 19, 20, 21]  # include/config.hpp:7-9
+    assert len(ids) == len(set(ids)) == L().swb_config_count()
+    for bad in (0, 999, 1000, -1, 2 ** 32 + 1):
+        assert not valid_config(bad)
+    ref_geom = {1: (1, 4, 2), 2: (2, 4, 2), 4: (4, 4, 2), 8: (8, 4, 2), 16: (1, 4, 8), 17: (2, 4, 8),
+                18: (4, 2, 8), 19: (1, 8, 8), 20: (2, 2, 8), 21: (4, 1, 8)}
+    for cid in ids:
+        c = config_info(cid)
+        assert c["id"] == cid
+        if c["family"] == _lib.SWB_FAMILY_LDG:
+            assert c["warps"] * c["rows"] * 32 <= 1024 and c["pack"] in (2, 8)
+            assert c["chunk"] == 0 and c["stages"] == 0
+        else:
+            assert c["family"] == _lib.SWB_FAMILY_BULK
+            assert c["chunk"] % 8 == 0 and c["stages"] >= 2 and (c["warps"] + 1) * 32 <= 1024
+        if cid in ref_geom:
+            assert (c["warps"], c["rows"], c["pack"]) == ref_geom[cid]
+    with pytest.raises(RuntimeError, match="unknown kernel configuration"):
+        config_info(999)
+
+
+def _msg():
+    return _lib.last_error()
+
+
+def test_gate_guards_in_reference_order():
+    f = L().swb_gate
+    assert f(1, None, FAKE, FAKE, None, None, FAKE, 4, 4, 0, None) == _lib.SWB_E_INPUT
+    assert f(1, FAKE, FAKE, FAKE, None, None, FAKE, 0, 4, 0, None) == _lib.SWB_E_INPUT
+    assert f(1, FAKE, FAKE, None, None, None, FAKE, 4, 4, 0, None) == _lib.SWB_E_INPUT
+    assert f(1, FAKE, None, FAKE, None, None, FAKE, 4, 4, 0, None) == _lib.SWB_E_GATE_BUFFERS
+    assert f(1, FAKE, FAKE, FAKE, None, None, None, 4, 4, 0, None) == _lib.SWB_E_GATE_BUFFERS
+    assert f(999, FAKE, FAKE, FAKE, None, None, FAKE, 4, 4, 0, None) == _lib.SWB_E_CONFIG
+    assert _msg() == "unknown kernel configuration"
+
+
+def test_project_guards_in_reference_order():
+    f = L().swb_project
+    assert f(1, None, FAKE, None, None, FAKE, 4, 4, 0, None) == _lib.SWB_E_INPUT
+    assert f(1, FAKE, FAKE, None, None, None, 4, 4, 0, None) == _lib.SWB_E_FLOAT_OUTPUT
+    assert f(1, FAKE, FAKE, None, None, None, 4, 4, _lib.SWB_HALF_OUT, None) == _lib.SWB_E_HALF_OUTPUT
+    assert f(1, FAKE, FAKE, None, None, FAKE, 4, 4, _lib.SWB_RESIDUAL, None) == _lib.SWB_E_RESIDUAL
+    assert f(0, FAKE, FAKE, None, None, FAKE, 4, 4, 0, None) == _lib.SWB_E_CONFIG
+
+
+def test_swiglu_out_guards_in_binding_order():
+    f = L().swb_swiglu_out
+    H, I = 64, 96
+    x, g, u, d, h, y = (FAKE + k * (1 << 24) for k in range(6))
+    assert f(x, g, u, d, h, y, 0, I, 1, 1, None) == _lib.SWB_E_SHAPE
+    assert f(x, g, u, d, h, y, H, 100001, 1, 1, None) == _lib.SWB_E_SHAPE
+    # configuration ids are range-checked before narrowing (torch_extension.cu:21-22)
+    assert f(x, g, u, d, h, y, H, I, 2 ** 32 + 1, 1, None) == _lib.SWB_E_CONFIG_RANGE
+    assert f(x, g, u, d, h, y, H, I, 1, -1, None) == _lib.SWB_E_CONFIG_RANGE
+    assert f(x, g, u, d, h, y, H, I, 0, 1, None) == _lib.SWB_E_CONFIG_INVALID
+    assert f(x, g, u, d, h, y, H, I, 1, 999, None) == _lib.SWB_E_CONFIG_INVALID
+    assert _msg() == "invalid configuration"
+    # aliasing: output onto the input x, h onto a weight, h onto y
+    assert f(x, g, u, d, h, x, H, I, 1, 1, None) == _lib.SWB_E_OVERLAP_INPUT
+    assert f(x, g, u, d, g + 10, y, H, I, 1, 1, None) == _lib.SWB_E_OVERLAP_INPUT
+    assert f(x, g, u, d, h, h + 2 * I - 2, H, I, 1, 1, None) == _lib.SWB_E_OVERLAP_OUTPUT
+    assert _msg() == "scratch and output overlap"
+    # adjacent but disjoint buffers are accepted by the alias guard (then fail null checks)
+    assert f(x, g, u, d, h, None, H, I, 1, 1, None) == _lib.SWB_E_HALF_OUTPUT
+
+
+def test_ffn_guards():
+    f = L().swb_ffn
+    assert f(1, 999, FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, FAKE, 8, 8, None) == _lib.SWB_E_CONFIG
+    assert f(1, 1, FAKE, FAKE, None, FAKE, None, None, None, FAKE, FAKE, 8, 8, None) == _lib.SWB_E_INPUT
+    assert f(1, 1, FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, None, 8, 8, None) == _lib.SWB_E_FLOAT_OUTPUT
+
+
+def test_epilogue_guards():
+    assert L().swb_gate_epilogue(None, FAKE, FAKE, FAKE, FAKE, 8, None) == _lib.SWB_E_INPUT
+    assert L().swb_residual_epilogue(FAKE, FAKE, FAKE, 0, None) == _lib.SWB_E_INPUT
+
+
+def test_binding_rejects_cpu_tensors_with_reference_message():
+    import torch
+    from swiglu_b200 import swiglu_out, swiglu
+    t = torch.zeros(4, dtype=torch.float16)
+    w = torch.zeros(4, 4, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="all buffers must be contiguous CUDA FP16 tensors"):
+        swiglu_out(t, w, w, w, t.clone(), t.clone(), 1, 1)
+    with pytest.raises(RuntimeError, match="gate must be a matrix"):
+        swiglu(t, t, w, w, 1)
+    with pytest.raises(TypeError):
+        swiglu_out(t, w, w, w, t, t, 2 ** 64, 1)
+
+
+def test_decode_swiglu_dropin_module():
+    import decode_swiglu as ext
+    from swiglu_b200 import binding
+    assert ext.swiglu_out is binding.swiglu_out and ext.swiglu is binding.swiglu
+    assert ext.config_ids() == binding.config_ids()

@@ -1,0 +1,258 @@
+"""GPU parity: every registry geometry against the CPU oracle, through the C ABI.
+
+Tolerances (stated here, checked per element):
+* relative error |a - e| / (|e| + atol), atol = 1e-3 * max|e|:
+  <= 1e-2 on fp16 h, <= 2e-3 on fp32 y;
+* and the reference's own gate (include/contract.hpp:36-53): atol 0.003, rtol 0.01.
+The model-rounding binding path is checked as tools/gpu_validate.py checks it
+(torch fp16 reference, atol .01, rtol .02) and against the oracle's fp16 path.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from swiglu_b200 import _lib, binding
+from swiglu_b200.binding import config_ids
+
+pytestmark = pytest.mark.gpu
+
+H_TOL = 1e-2
+Y_TOL = 2e-3
+
+CORRECTNESS = [(1, 1), (37, 65), (129, 257), (512, 1024), (1, 9), (2, 3), (8, 8), (7, 9), (9, 7), (31, 33),
+               (32, 32), (33, 31), (64, 64), (66, 70), (256, 256), (264, 272), (1024, 256), (1025, 513),
+               (1030, 514)]
+BASELINE_SHAPES = [(17, 33), (2047, 5631), (2048, 5632), (2048, 8192), (4096, 11008), (4096, 14336)]
+
+
+def rel_err(actual, expected):
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    atol = 1e-3 * max(float(np.max(np.abs(e))), 1e-30)
+    return float(np.max(np.abs(a - e) / (np.abs(e) + atol)))
+
+
+def dev(a, offset=0):
+    """Upload a float16/float32 numpy array; offset>0 places it `offset` elements past an aligned start."""
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if offset:
+        backing = torch.empty(t.numel() + offset, dtype=t.dtype, device="cuda")
+        out = backing[offset:].view(t.shape)
+        out.copy_(t)
+        return out
+    return t.cuda()
+
+
+class Case:
+    def __init__(self, hidden, inter, dist="normal", x_offset=0, w_offset=0):
+        self.hidden, self.inter = hidden, inter
+        w = O.normal_workload(0, hidden, inter) if dist == "normal" else O.reference_workload(17, hidden, inter)
+        self.w = w
+        self.proj, self.act, self.y = O.ffn(w)
+        self.d = {k: dev(v, w_offset if k in ("wg", "wu", "wd") else (x_offset if k == "x" else 0))
+                  for k, v in w.items()}
+        self.act_d = dev(self.act)
+        # down-kernel reference on the oracle's own h: isolates the down kernel
+        self.y_down = O.project(w["wd"], self.act, w["bd"], w["x"])
+
+    def gate(self, cfg):
+        h = torch.empty(self.inter, dtype=torch.float16, device="cuda")
+        d = self.d
+        binding.gate(d["wg"], d["wu"], d["x"], h, cfg, d["bg"], d["bu"])
+        return h
+
+    def down(self, cfg):
+        y = torch.empty(self.hidden, dtype=torch.float32, device="cuda")
+        binding.project(self.d["wd"], self.act_d, y, cfg, bias=self.d["bd"], residual=self.d["x"])
+        return y
+
+
+def check_gate(case, h):
+    h = h.cpu().numpy()
+    assert np.isfinite(h).all()
+    assert rel_err(h, case.act) <= H_TOL
+
+
+def check_down(case, y):
+    y = y.cpu().numpy()
+    assert rel_err(y, case.y_down) <= Y_TOL
+    assert O.compare(y, case.y_down)[0]
+
+
+@pytest.fixture(scope="module")
+def ids():
+    return config_ids()
+
+
+@pytest.mark.parametrize("shape", CORRECTNESS)
+def test_correctness_suite_every_config(shape, ids):
+    case = Case(*shape, dist="uniform")
+    for cfg in ids:
+        check_gate(case, case.gate(cfg))
+        check_down(case, case.down(cfg))
+    torch.cuda.synchronize()
+    assert binding.device_error() == 0
+
+
+@pytest.mark.parametrize("shape", BASELINE_SHAPES)
+def test_baseline_shapes_every_config(shape, ids):
+    case = Case(*shape)
+    for cfg in ids:
+        check_gate(case, case.gate(cfg))
+        check_down(case, case.down(cfg))
+    assert binding.device_error() == 0
+
+
+@pytest.mark.parametrize("shape,x_off,w_off", [((2048, 5632), 1, 0), ((2047, 5631), 1, 0), ((17, 33), 1, 0),
+                                               ((256, 264), 0, 1), ((2048, 5632), 1, 1), ((66, 70), 3, 5)])
+def test_misaligned_inputs_every_config(shape, x_off, w_off, ids):
+    case = Case(*shape, x_offset=x_off, w_offset=w_off)
+    assert case.d["x"].data_ptr() % 16 != 0 or x_off == 0
+    for cfg in ids:
+        check_gate(case, case.gate(cfg))
+        check_down(case, case.down(cfg))
+
+
+@pytest.mark.parametrize("shape", [(37, 65), (2048, 5632), (4096, 14336)])
+def test_full_layer_matches_reference_oracle(shape, ids):
+    case = Case(*shape)
+    d = case.d
+    pairs = [(g, dd) for g in ids for dd in ids if g == dd or {g, dd} & {33, 64, 65}]
+    for g, dd in pairs:
+        h = torch.empty(case.inter, dtype=torch.float16, device="cuda")
+        y = torch.empty(case.hidden, dtype=torch.float32, device="cuda")
+        binding.ffn(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, g, dd)
+        assert rel_err(h.cpu().numpy(), case.act) <= H_TOL, (g, dd)
+        yc = y.cpu().numpy()
+        assert rel_err(yc, case.y) <= Y_TOL, (g, dd)
+        assert O.compare(yc, case.y)[0], (g, dd)
+
+
+def test_reference_golden_uniform_workload(ids):
+    """The reference's own seed-17 workload: y within the reference's gate of its stored outputs."""
+    data = np.load(O.HERE.parent / "tests" / "golden" / "reference_small.npz")
+    names = sorted({k.split("/")[0] for k in data.files})
+    for name in names:
+        w = {k: data[f"{name}/{k}"].view(np.float16) for k in ("wg", "wu", "wd", "x", "bg", "bu", "bd")}
+        d = {k: dev(v) for k, v in w.items()}
+        inter, hidden = w["wg"].shape
+        for cfg in (1, 16, 33, 64):
+            h = torch.empty(inter, dtype=torch.float16, device="cuda")
+            y = torch.empty(hidden, dtype=torch.float32, device="cuda")
+            binding.ffn(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, cfg, cfg)
+            assert O.compare(y.cpu().numpy(), data[f"{name}/y"])[0], (name, cfg)
+
+
+def test_raw_projection_fp32(ids):
+    case = Case(2048, 8192)
+    for cfg in ids:
+        g = torch.empty(8192, dtype=torch.float32, device="cuda")
+        binding.project(case.d["wg"], case.d["x"], g, cfg)
+        gc = g.cpu().numpy()
+        assert rel_err(gc, case.proj) <= Y_TOL
+        assert O.compare(gc, case.proj)[0]
+
+
+def test_half_output_projection(ids):
+    case = Case(512, 1024)
+    expect = O.project(case.w["wd"], case.act, half_out=True)
+    for cfg in ids:
+        out = torch.empty(512, dtype=torch.float16, device="cuda")
+        binding.project(case.d["wd"], case.act_d, out, cfg)
+        assert rel_err(out.cpu().numpy(), expect) <= H_TOL
+
+
+def test_deterministic_across_runs(ids):
+    case = Case(4096, 11008)
+    for cfg in ids:
+        a, b = case.gate(cfg), case.gate(cfg)
+        assert torch.equal(a, b)
+        ya, yb = case.down(cfg), case.down(cfg)
+        assert torch.equal(ya, yb)
+
+
+# ---- the drop-in binding (tools/gpu_validate.py semantics) --------------------
+
+@pytest.mark.parametrize("hidden,inter", [(1, 1), (7, 9), (8, 8), (31, 33), (64, 70), (256, 264), (513, 1025)])
+def test_binding_every_pair_aligned_and_misaligned(hidden, inter, ids):
+    torch.manual_seed(101)
+    with torch.inference_mode():
+        weights = [torch.randn((inter, hidden), device="cuda", dtype=torch.float16) / hidden ** .5,
+                   torch.randn((inter, hidden), device="cuda", dtype=torch.float16) / hidden ** .5,
+                   torch.randn((hidden, inter), device="cuda", dtype=torch.float16) / inter ** .5]
+        for offset in (0, 1):
+            backing = torch.randn((hidden + offset,), device="cuda", dtype=torch.float16)
+            x = backing[offset:].view(1, 1, hidden)
+            expected = (torch.nn.functional.silu(x @ weights[0].T) * (x @ weights[1].T)) @ weights[2].T
+            h = torch.empty((inter,), device="cuda", dtype=torch.float16)
+            y = torch.empty_like(x)
+            for g in ids:
+                for d in ids:
+                    binding.swiglu_out(x, *weights, h, y, g, d)
+                    torch.testing.assert_close(y, expected, atol=.01, rtol=.02)
+            with pytest.raises(RuntimeError, match="workspace overlaps input storage"):
+                binding.swiglu_out(x, *weights, h, x, 1, 1)
+            for invalid in (0, 999, 2 ** 32 + 1):
+                with pytest.raises(RuntimeError):
+                    binding.swiglu_out(x, *weights, h, y, invalid, 1)
+
+
+def test_binding_matches_oracle_model_rounding(ids):
+    w = O.normal_workload(4, 2048, 5632)
+    h_ref, y_ref = O.ffn_model(w)
+    d = {k: dev(v) for k, v in w.items()}
+    x = d["x"].view(1, 1, -1)
+    h = torch.empty(5632, dtype=torch.float16, device="cuda")
+    y = torch.empty_like(x)
+    for cfg in ids:
+        binding.swiglu_out(x, d["wg"], d["wu"], d["wd"], h, y, cfg, cfg)
+        hc = h.cpu().numpy()
+        # fp16 rounding points match; differences are at most a couple of ulps
+        assert rel_err(hc, h_ref) <= H_TOL
+        assert np.mean(hc.view(np.uint16) == h_ref.view(np.uint16)) > 0.97
+        assert rel_err(y.cpu().numpy().ravel(), y_ref) <= H_TOL
+
+
+def test_swiglu_allocating_wrapper():
+    w = O.normal_workload(5, 256, 512)
+    d = {k: dev(v) for k, v in w.items()}
+    x = d["x"].view(1, 1, -1)
+    y1 = binding.swiglu(x, d["wg"], d["wu"], d["wd"], 33)
+    h = torch.empty(512, dtype=torch.float16, device="cuda")
+    y2 = torch.empty_like(x)
+    binding.swiglu_out(x, d["wg"], d["wu"], d["wd"], h, y2, 33, 33)
+    assert torch.equal(y1, y2)
+
+
+def test_binding_inside_cuda_graph():
+    w = O.normal_workload(6, 2048, 5632)
+    d = {k: dev(v) for k, v in w.items()}
+    x = d["x"].view(1, 1, -1)
+    h = torch.empty(5632, dtype=torch.float16, device="cuda")
+    y = torch.empty_like(x)
+    for cfg in (16, 33, 64):
+        binding.swiglu_out(x, d["wg"], d["wu"], d["wd"], h, y, cfg, cfg)
+        eager = y.clone()
+        y.zero_()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            binding.swiglu_out(x, d["wg"], d["wu"], d["wd"], h, y, cfg, cfg)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y, eager)
+
+
+def test_cublas_baseline_matches_oracle():
+    case = Case(2048, 5632)
+    d = case.d
+    base = binding.CublasBaseline()
+    g = torch.empty(5632, dtype=torch.float32, device="cuda")
+    u = torch.empty_like(g)
+    h = torch.empty(5632, dtype=torch.float16, device="cuda")
+    y = torch.empty(2048, dtype=torch.float32, device="cuda")
+    for algo in (0, 1):
+        base.ffn(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], g, u, h, y, algo=algo)
+        assert O.compare(y.cpu().numpy(), case.y)[0]
+        assert rel_err(h.cpu().numpy(), case.act) <= H_TOL
+    base.close()
