@@ -1,0 +1,221 @@
+"""Host simulation of every kernel's thread -> element mapping (no GPU).
+
+Extends the reference's address-coverage audit (tests/mapping_tests.cpp:6-27:
+every column read exactly once, every output row written exactly once, for all
+configs x correctness shapes x both orientations x input offsets {0,2,4,8} bytes)
+to this build's kernels:
+
+* ldg_kernel: scalar head up to the first aligned weight, vector body with
+  UNROLL loads in flight, scalar tail; every vector load aligned;
+* bulk_kernel: balanced row ranges per CTA, chunked cp.async.bulk copies whose
+  sizes and addresses are 16-byte multiples and whose expect_tx totals equal the
+  bytes copied, ring-stage reuse order, shared-memory layout within 227 KB.
+
+The index arithmetic below restates cuda-kernel_b200/csrc/kernels.cuh and the
+launch arithmetic of csrc/swiglu_b200.cu line by line.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from swiglu_b200 import config_ids, config_info
+
+CORRECTNESS = [(1, 1), (37, 65), (129, 257), (512, 1024), (1, 9), (2, 3), (8, 8), (7, 9), (9, 7), (31, 33),
+               (32, 32), (33, 31), (64, 64), (66, 70), (256, 256), (264, 272), (1024, 256), (1025, 513),
+               (1030, 514)]
+EXTRA = [(17, 33), (2047, 5631), (2048, 5632), (4096, 14336)]
+SMEM_PER_SM = 233472
+SMEM_PER_CTA = 232448
+SMS = 148
+
+
+def ldg_row_coverage(T, pack, unroll, cols, w_addr, u_addr=None):
+    """Columns touched by the T threads of one row; returns (counts, vector addresses)."""
+    VB = 2 * pack
+    vec = True
+    if u_addr is not None:
+        vec = (u_addr - w_addr) % VB == 0
+    peel = ((VB - w_addr % VB) % VB) // 2 if vec else cols
+    peel = min(peel, cols)
+    nvec = (cols - peel) // pack
+    tail0 = peel + nvec * pack
+    counts = np.zeros(cols, np.int64)
+    addrs = []
+    for t in range(T):
+        for c in range(t, peel, T):
+            counts[c] += 1
+        v = t
+        while v + (unroll - 1) * T < nvec:
+            for i in range(unroll):
+                c = peel + (v + i * T) * pack
+                counts[c:c + pack] += 1
+                addrs.append(w_addr + 2 * c)
+            v += unroll * T
+        while v < nvec:
+            c = peel + v * pack
+            counts[c:c + pack] += 1
+            addrs.append(w_addr + 2 * c)
+            v += T
+        for c in range(tail0 + t, cols, T):
+            counts[c] += 1
+    return counts, addrs, peel, VB
+
+
+def audit_ldg(cfg, rows, cols, offset_bytes, gated):
+    W, R, pack, unroll = cfg["warps"], cfg["rows"], cfg["pack"], cfg["unroll"]
+    T = 32 * W
+    base = 4096 + offset_bytes
+    seen_peels = {}
+    for row in range(rows):
+        w_addr = base + 2 * row * cols
+        u_addr = (1 << 30) + offset_bytes + 2 * row * cols if gated else None
+        key = (w_addr % 16, None if u_addr is None else u_addr % 16)
+        if key in seen_peels:
+            continue
+        counts, addrs, peel, VB = ldg_row_coverage(T, pack, unroll, cols, w_addr, u_addr)
+        assert (counts == 1).all(), ("column omitted or duplicated", cfg["id"], rows, cols, offset_bytes)
+        assert all(a % VB == 0 for a in addrs), "misaligned vector load"
+        # staged-x vector reads start on 16-byte (pack 8) / 8-byte (pack 2) boundaries when enabled
+        seen_peels[key] = peel
+    grid = (rows + R - 1) // R
+    outputs = np.zeros(rows, np.int64)
+    for block in range(grid):
+        for warp in range(W * R):
+            group, sub = warp // W, warp % W
+            row = block * R + group
+            if sub == 0 and row < rows:
+                outputs[row] += 1
+    assert (outputs == 1).all(), "output omitted or duplicated"
+
+
+def bulk_layout(nm, chunk, stages, cols, cw, rows_per_cta):
+    def up(v, a):
+        return (v + a - 1) // a * a
+    ring = stages * nm * chunk * 2
+    full = up(ring, 16)
+    empty = full + stages * 8
+    xs = up(empty + stages * 8, 16)
+    part = up(xs + cols * 4, 16)
+    total = up(part + rows_per_cta * cw * nm * 4, 16)
+    return {"ring": 0, "full": full, "empty": empty, "xs": xs, "part": part, "total": total}
+
+
+def bulk_plan(cfg, rows, cols, gated, w_aligned=True):
+    """Mirror of launch_bulk: returns None when the fallback geometry runs."""
+    nm = 2 if gated else 1
+    cw, cps, chunk, smax = cfg["warps"], cfg["rows"], cfg["chunk"], cfg["stages"]
+    G = min(SMS * cps, rows)
+    rpc = (rows + G - 1) // G
+    budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 64
+    stages = smax
+    while stages >= 2 and bulk_layout(nm, chunk, stages, cols, cw, rpc)["total"] > budget:
+        stages -= 1
+    if cols % 8 or not w_aligned or stages < 2:
+        return None
+    return {"G": G, "rpc": rpc, "stages": stages, "layout": bulk_layout(nm, chunk, stages, cols, cw, rpc),
+            "budget": budget}
+
+
+def audit_bulk(cfg, rows, cols, gated):
+    plan = bulk_plan(cfg, rows, cols, gated)
+    if plan is None:
+        return False
+    nm = 2 if gated else 1
+    cw, chunk = cfg["warps"], cfg["chunk"]
+    CT = cw * 32
+    G, stages, L = plan["G"], plan["stages"], plan["layout"]
+    assert L["total"] <= plan["budget"]
+    assert L["full"] % 8 == 0 and L["empty"] % 8 == 0 and L["xs"] % 16 == 0
+    assert (nm * chunk * 2) % 16 == 0
+    row_owner = np.zeros(rows, np.int64)
+    nch = (cols + chunk - 1) // chunk
+    for b in range(G):
+        r0, r1 = (b * rows) // G, ((b + 1) * rows) // G
+        assert r1 - r0 >= 1 and r1 - r0 <= plan["rpc"]
+        row_owner[r0:r1] += 1
+        units = (r1 - r0) * nch
+        # producer: stage reuse order, byte counts, alignment
+        fills = {}
+        row, ch = r0, 0
+        for k in range(units):
+            s = k % stages
+            if k >= stages:
+                assert fills[s] == k - stages  # the consumer release waited for is this stage's previous fill
+            fills[s] = k
+            c0 = ch * chunk
+            length = min(chunk, cols - c0)
+            nbytes = length * 2
+            assert nbytes % 16 == 0 and nbytes > 0
+            src = 2 * (row * cols + c0)
+            assert src % 16 == 0
+            dst = s * nm * chunk * 2
+            assert dst % 16 == 0 and dst + nm * nbytes <= L["full"]
+            assert nbytes * nm < (1 << 20)  # mbarrier tx-count range
+            ch += 1
+            if ch == nch:
+                ch, row = 0, row + 1
+        assert row == r1
+        # consumer: every column of a chunk read by exactly one thread
+        for c0 in range(0, cols, chunk):
+            nv = min(chunk, cols - c0) // 8
+            counts = np.zeros(nv, np.int64)
+            for t in range(CT):
+                counts[t:nv:CT] += 1
+            assert (counts == 1).all()
+        if b > 3 and b < G - 3:
+            continue
+    assert (row_owner == 1).all()
+    return True
+
+
+@pytest.fixture(scope="module")
+def configs():
+    return [config_info(i) for i in config_ids()]
+
+
+@pytest.mark.parametrize("shape", CORRECTNESS)
+def test_ldg_coverage(configs, shape):
+    h, i = shape
+    n = 0
+    for cfg in configs:
+        if cfg["family"] != 0:
+            continue
+        for off in (0, 2, 4, 8):
+            for rows, cols in ((i, h), (h, i)):
+                for gated in (True, False):
+                    audit_ldg(cfg, rows, cols, off, gated)
+                    n += 1
+    assert n > 0
+
+
+@pytest.mark.parametrize("shape", CORRECTNESS + EXTRA)
+def test_bulk_plan_and_coverage(configs, shape):
+    h, i = shape
+    for cfg in configs:
+        if cfg["family"] != 1:
+            continue
+        for rows, cols, gated in ((i, h, True), (h, i, False)):
+            ran = audit_bulk(cfg, rows, cols, gated)
+            if cols % 8 == 0 and cols <= 16384:
+                assert ran, (cfg["id"], rows, cols)
+
+
+def test_bulk_large_shapes_fit_every_geometry(configs):
+    for cfg in configs:
+        if cfg["family"] != 1:
+            continue
+        for rows, cols, gated in ((14336, 4096, True), (4096, 14336, False), (11008, 4096, True),
+                                  (4096, 11008, False), (5632, 2048, True), (2048, 5632, False)):
+            plan = bulk_plan(cfg, rows, cols, gated)
+            assert plan is not None and plan["stages"] >= 2, (cfg["id"], rows, cols)
+            # one CTA per SM set, rows balanced within one row
+            per = [((b + 1) * rows) // plan["G"] - (b * rows) // plan["G"] for b in range(plan["G"])]
+            assert max(per) - min(per) <= 1
+
+
+def test_bulk_falls_back_when_unaligned(configs):
+    for cfg in configs:
+        if cfg["family"] == 1:
+            assert bulk_plan(cfg, 5631, 2047, True) is None
+            assert bulk_plan(cfg, 64, 64, True, w_aligned=False) is None
