@@ -262,9 +262,16 @@ def ours(args) -> None:
             gcfg, dcfg = int(t[0]), int(t[1])
 
     def step(i):
-        launch_gate(gcfg, i)
-        launch_down(dcfg, i)
-        if world > 1:
+        # the layer entry points: gate kernel, then the down kernel launched programmatically
+        s = sets[i % copies]
+        if world == 1:
+            _lib.check(L.swb_ffn(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                 x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
+                                 y.data_ptr(), H, shard, sp))
+        else:
+            _lib.check(L.swb_ffn_tp(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                    x.data_ptr(), bg.data_ptr(), bu.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard,
+                                    sp))
             dist.all_reduce(y)
             _lib.check(L.swb_residual_epilogue(y.data_ptr(), bd.data_ptr(), x.data_ptr(), H, sp))
 
@@ -284,41 +291,38 @@ def ours(args) -> None:
         raise SystemExit(f"bench sanity check failed on rank {rank}: max relative error {rel}")
     launches_per_step = 2 if world == 1 else 3
 
-    # ---- CUDA graphs for the tensor-parallel step (launch overhead would dominate)
-    graphs = None
-    if world > 1:
-        graphs = []
-        for c in range(copies):
-            step(c)  # warm NCCL before capture
-        torch.cuda.synchronize()
-        for c in range(copies):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                step(c)
-            graphs.append(g)
-        torch.cuda.synchronize()
+    # ---- one CUDA graph per rotating copy holds the whole step (as the reference
+    # times its candidates: src/benchmark.cu:46-83); for N > 1 it includes the NCCL all-reduce
+    for c in range(copies):
+        step(c)  # warm every copy (and NCCL) before capture
+    torch.cuda.synchronize()
+    graphs = []
+    for c in range(copies):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(c)
+        graphs.append(g)
+    torch.cuda.synchronize()
 
     def run_step(i):
-        if graphs is None:
-            step(i)
-        else:
-            graphs[i % copies].replay()
+        graphs[i % copies].replay()
 
-    sampler = ClockSampler(local).start()
+    sampler = ClockSampler(local, interval_s=0.002).start()
     for i in range(args.warmup):
         run_step(i)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    t_window = [time.time()]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for i in range(args.steps):
         run_step(i)
     end.record(stream)
     end.synchronize()
+    t_window.append(time.time())
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
     elapsed_ms = start.elapsed_time(end)
     if world > 1:
         t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
@@ -357,31 +361,41 @@ def ours(args) -> None:
         tp = {"ranks": world, "shard_rows": shard, "allreduce_us": float(t.item()), "allreduce_bytes": H * 4,
               "backend": "nccl"}
 
-    # ---- end to end through the public C-ABI call with host buffers (rank 0 path at N=1)
+    # ---- end to end through the public C-ABI call with host buffers (N=1). As the
+    # reference's transfer-inclusive timing (src/benchmark.cu:177-206): each step copies
+    # x from pinned host memory, runs the captured layer call, copies y back to pinned host.
     e2e = None
     if world == 1:
         x_host = common["x"].cpu().pin_memory()
         y_host = torch.empty(H, dtype=torch.float32).pin_memory()
         x_dev = torch.empty_like(x)
-        for i in range(3):
-            x_dev.copy_(x_host, non_blocking=True)
-            binding.ffn(x_dev, sets[i % copies]["wg"], sets[i % copies]["wu"], sets[i % copies]["wd"], bg, bu, bd, h, y,
-                        gcfg, dcfg, stream=sp)
-            y_host.copy_(y, non_blocking=True)
+        e2e_graphs = []
+        for c in range(copies):
+            binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg, stream=sp)
         torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for i in range(args.steps):
-            s = sets[i % copies]
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg,
+                            stream=sp)
+            e2e_graphs.append(g)
+
+        def e2e_step(i):
             x_dev.copy_(x_host, non_blocking=True)
-            binding.ffn(x_dev, s["wg"], s["wu"], s["wd"], bg, bu, bd, h, y, gcfg, dcfg, stream=sp)
+            e2e_graphs[i % copies].replay()
             y_host.copy_(y, non_blocking=True)
-        b.record(stream)
-        b.synchronize()
-        e2e = {"value": a.elapsed_time(b) * 1e3 / args.steps, "unit": UNIT,
+
+        for i in range(max(args.warmup, 3)):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        e2e_us = time_kernel(torch, e2e_step, args.steps, stream)
+        if not torch.equal(y_host, y.cpu()):
+            raise SystemExit("end-to-end output mismatch")
+        e2e = {"value": e2e_us, "unit": UNIT,
                "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
-               "path": "swb_ffn via swiglu_b200.binding.ffn, pinned host x -> device -> pinned host y"}
+               "path": "pinned host x -> H2D -> captured swb_ffn (C ABI) -> D2H -> pinned host y"}
+        del e2e_graphs
 
     # ---- cuBLAS GemmEx + pointwise on the same GPU (baseline, N=1)
     cublas = None
@@ -393,16 +407,30 @@ def ours(args) -> None:
         yb = torch.empty(H, dtype=torch.float32, device=device)
         res = {}
         for algo in (0, 1):
-            fn = lambda i, a=algo: base.ffn(x, sets[i % copies]["wg"], sets[i % copies]["wu"],  # noqa: E731
-                                            sets[i % copies]["wd"], bg, bu, bd, gbuf, ubuf, hb, yb, algo=a, stream=sp)
+            # warm (cuBLAS workspaces), capture one graph per copy, time replays -- the same
+            # protocol as our layer (src/benchmark.cu:46-83)
+            cg = []
+            for c in range(copies):
+                base.ffn(x, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, gbuf, ubuf, hb, yb, algo=algo,
+                         stream=sp)
+            torch.cuda.synchronize()
+            for c in range(copies):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    base.ffn(x, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, gbuf, ubuf, hb, yb,
+                             algo=algo, stream=sp)
+                cg.append(g)
+            fn = lambda i, cg=cg: cg[i % copies].replay()  # noqa: E731
             for i in range(args.warmup):
                 fn(i)
             res[algo] = time_kernel(torch, fn, args.steps, stream)
+            del cg
         algo = min(res, key=res.get)
         cublas = {"value": res[algo], "unit": UNIT, "algo": ["default", "default_tensor_op"][algo],
                   "kernels_per_step": 5, "speedup_vs_cublas": res[algo] / us_per_layer}
         base.close()
 
+    clocks = sampler.stop(window=tuple(t_window))
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(sets, common, H, I, args.cpu_seconds)

@@ -115,6 +115,15 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
         : "memory");
 }
 
+// Programmatic dependent launch. launch_dependents lets the next kernel in the
+// stream (launched with the programmatic-serialization attribute) start early;
+// wait blocks until every kernel this one depends on has completed and its
+// memory is visible. Both are no-ops when no programmatic dependency exists.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier among the first `threads` threads of the CTA (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -115,6 +115,51 @@ __device__ __forceinline__ float load_x1(const Params& p, const float* xs, int c
     return p.x_staged ? xs[c] : __half2float(p.x[c]);
 }
 
+// Copies x[0, cols) into shared memory as fp32 using threads [tid, nthreads).
+// 16-byte loads when x is 16-byte aligned, four loads in flight per thread, so
+// a 14336-element x costs one or two L2 round trips rather than dozens.
+__device__ __forceinline__ void stage_x(const __half* __restrict__ x, float* xs, int cols, int tid, int nthreads) {
+    constexpr int U = 4;
+    int tail = 0;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int nv = cols / 8;
+        const uint4* xv = reinterpret_cast<const uint4*>(x);
+        for (int v = tid; v < nv; v += U * nthreads) {
+            uint4 a[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i)
+                if (v + i * nthreads < nv) a[i] = xv[v + i * nthreads];
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+                const int vi = v + i * nthreads;
+                if (vi < nv) {
+                    const uint32_t w[4] = {a[i].x, a[i].y, a[i].z, a[i].w};
+                    float f[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 p2 = half2_bits_to_float2(w[k]);
+                        f[2 * k] = p2.x;
+                        f[2 * k + 1] = p2.y;
+                    }
+                    float4* dst = reinterpret_cast<float4*>(xs + vi * 8);
+                    dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+                    dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+                }
+            }
+        }
+        tail = nv * 8;
+    }
+    for (int c = tail + tid; c < cols; c += U * nthreads) {
+        float f[U];
+#pragma unroll
+        for (int i = 0; i < U; ++i)
+            if (c + i * nthreads < cols) f[i] = __half2float(x[c + i * nthreads]);
+#pragma unroll
+        for (int i = 0; i < U; ++i)
+            if (c + i * nthreads < cols) xs[c + i * nthreads] = f[i];
+    }
+}
+
 // ======================================================================= LDG
 
 template <int WPR, int ROWS, int PACK, int UNROLL, int MODE>
@@ -131,8 +176,11 @@ __global__ void __launch_bounds__(32 * WPR * ROWS) ldg_kernel(const Params p) {
     __shared__ float red[NM][ROWS * WPR];
 
     const int cols = p.cols;
+    griddep_launch_dependents();
+    // x may be the previous kernel's output (h of the gate stage).
+    griddep_wait();
     if (p.x_staged) {
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) xs[c] = __half2float(p.x[c]);
+        stage_x(p.x, xs, cols, threadIdx.x, blockDim.x);
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -302,9 +350,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
         }
         mbar_fence_init();
     }
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) xs[c] = __half2float(p.x[c]);
     __syncthreads();
+    griddep_launch_dependents();
 
+    // The producer starts streaming weights at once (it never reads x); the
+    // consumers stage x meanwhile and meet at a named barrier before reading it.
     if (warp == CW) {
         // ------------------------------------------------------- producer
         if (lane != 0) return;
@@ -336,6 +386,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
 
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
+    griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
+    stage_x(p.x, xs, cols, t, CT);
+    named_barrier_sync(1, CT);
     float acc[NM][4];
 #pragma unroll
     for (int m = 0; m < NM; ++m)

@@ -102,23 +102,47 @@ int ensure_smem(Kernel kernel, std::atomic<uint64_t>& done_mask, size_t bytes) {
     return SWB_OK;
 }
 
+// Launches `kernel`; with `pdl` the launch may begin before the previous kernel
+// in the stream finishes (programmatic dependent launch). Only used for the
+// down projection right after this library's own gate kernel: the down kernel
+// reads nothing the gate writes until its griddepcontrol.wait.
+template <typename Kernel>
+void launch_kernel(Kernel kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t stream, bool pdl,
+                   const Params& p) {
+    if (!pdl) {
+        kernel<<<grid, block, smem, stream>>>(p);
+        return;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 template <int W, int R, int PK, int U, int MODE>
-int launch_ldg(Params p, cudaStream_t stream) {
+int launch_ldg(Params p, cudaStream_t stream, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
     p.x_staged = size_t(p.cols) * 4 <= kXStageLimit;
     const size_t smem = p.x_staged ? align_up(size_t(p.cols) * 4, 16) : 0;
     auto kernel = ldg_kernel<W, R, PK, U, MODE>;
     if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
     const unsigned grid = unsigned((p.rows + R - 1) / R);
-    kernel<<<grid, 32 * W * R, smem, stream>>>(p);
+    launch_kernel(kernel, grid, 32 * W * R, smem, stream, pdl, p);
     return check_launch();
 }
 
 template <int CW, int CPS, int CH, int ST, int MODE>
-int launch_bulk(Params p, cudaStream_t stream);
+int launch_bulk(Params p, cudaStream_t stream, bool pdl);
 
 template <int MODE>
-int run_fallback(Params p, cudaStream_t stream);
+int run_fallback(Params p, cudaStream_t stream, bool pdl);
 
 template <int FAM, int W, int R, int PK, int U, int CH, int ST>
 struct Launcher;
@@ -126,21 +150,21 @@ struct Launcher;
 template <int W, int R, int PK, int U, int CH, int ST>
 struct Launcher<SWB_FAM_LDG, W, R, PK, U, CH, ST> {
     template <int MODE>
-    static int run(Params p, cudaStream_t s) {
-        return launch_ldg<W, R, PK, U, MODE>(p, s);
+    static int run(Params p, cudaStream_t s, bool pdl) {
+        return launch_ldg<W, R, PK, U, MODE>(p, s, pdl);
     }
 };
 
 template <int W, int R, int PK, int U, int CH, int ST>
 struct Launcher<SWB_FAM_BULK, W, R, PK, U, CH, ST> {
     template <int MODE>
-    static int run(Params p, cudaStream_t s) {
-        return launch_bulk<W, R, CH, ST, MODE>(p, s);
+    static int run(Params p, cudaStream_t s, bool pdl) {
+        return launch_bulk<W, R, CH, ST, MODE>(p, s, pdl);
     }
 };
 
 template <int CW, int CPS, int CH, int ST, int MODE>
-int launch_bulk(Params p, cudaStream_t stream) {
+int launch_bulk(Params p, cudaStream_t stream, bool pdl) {
     constexpr int NM = MODE == MODE_GATE ? 2 : 1;
     static std::atomic<uint64_t> smem_set{0};
     const bool aligned = (p.cols % 8) == 0 && (reinterpret_cast<uintptr_t>(p.w) % 16) == 0 &&
@@ -152,22 +176,22 @@ int launch_bulk(Params p, cudaStream_t stream) {
     const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 64;
     int stages = ST;
     while (stages >= 2 && bulk_layout(NM, CH, stages, p.cols, CW, rows_per_cta).total > budget) --stages;
-    if (!aligned || stages < 2) return run_fallback<MODE>(p, stream);
+    if (!aligned || stages < 2) return run_fallback<MODE>(p, stream, pdl);
     p.stages = stages;
     p.x_staged = 1;
     const size_t smem = bulk_layout(NM, CH, stages, p.cols, CW, rows_per_cta).total;
     auto kernel = bulk_kernel<CW, CH, MODE>;
     if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
-    kernel<<<unsigned(G), (CW + 1) * 32, smem, stream>>>(p);
+    launch_kernel(kernel, unsigned(G), (CW + 1) * 32, smem, stream, pdl, p);
     return check_launch();
 }
 
 template <int MODE>
-int dispatch(int64_t id, const Params& p, cudaStream_t s) {
+int dispatch(int64_t id, const Params& p, cudaStream_t s, bool pdl = false) {
     switch (id) {
 #define SWB_CASE(ID, FAM, W, R, PK, U, CH, ST) \
     case ID:                                   \
-        return Launcher<FAM, W, R, PK, U, CH, ST>::template run<MODE>(p, s);
+        return Launcher<FAM, W, R, PK, U, CH, ST>::template run<MODE>(p, s, pdl);
         SWB_CONFIGS(SWB_CASE)
 #undef SWB_CASE
         default:
@@ -176,8 +200,8 @@ int dispatch(int64_t id, const Params& p, cudaStream_t s) {
 }
 
 template <int MODE>
-int run_fallback(Params p, cudaStream_t stream) {
-    return dispatch<MODE>(SWB_BULK_FALLBACK_ID, p, stream);
+int run_fallback(Params p, cudaStream_t stream, bool pdl) {
+    return dispatch<MODE>(SWB_BULK_FALLBACK_ID, p, stream, pdl);
 }
 
 bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {
@@ -258,8 +282,10 @@ int swb_gate(int config, const void* wg, const void* wu, const void* x, const vo
     return dispatch<MODE_GATE>(config, p, static_cast<cudaStream_t>(stream));
 }
 
-int swb_project(int config, const void* w, const void* x, const void* bias, const void* residual, void* out,
-                int rows, int cols, unsigned flags, void* stream) {
+namespace {
+// swb_project with an optional programmatic dependent launch (see launch_kernel).
+int project_impl(int config, const void* w, const void* x, const void* bias, const void* residual, void* out,
+                 int rows, int cols, unsigned flags, void* stream, bool pdl) {
     if (rows <= 0 || cols <= 0 || !w || !x) return fail(SWB_E_INPUT);
     const bool half_out = (flags & SWB_HALF_OUT) != 0;
     if (!out) return fail(half_out ? SWB_E_HALF_OUTPUT : SWB_E_FLOAT_OUTPUT);
@@ -275,10 +301,16 @@ int swb_project(int config, const void* w, const void* x, const void* bias, cons
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (half_out) {
         p.h = static_cast<__half*>(out);
-        return dispatch<MODE_F16>(config, p, s);
+        return dispatch<MODE_F16>(config, p, s, pdl);
     }
     p.y = static_cast<float*>(out);
-    return dispatch<MODE_F32>(config, p, s);
+    return dispatch<MODE_F32>(config, p, s, pdl);
+}
+}  // namespace
+
+int swb_project(int config, const void* w, const void* x, const void* bias, const void* residual, void* out,
+                int rows, int cols, unsigned flags, void* stream) {
+    return project_impl(config, w, x, bias, residual, out, rows, cols, flags, stream, false);
 }
 
 int swb_ffn(int gate_config, int down_config, const void* wg, const void* wu, const void* wd, const void* x,
@@ -288,7 +320,18 @@ int swb_ffn(int gate_config, int down_config, const void* wg, const void* wu, co
     if (!wd) return fail(SWB_E_INPUT);
     if (!y) return fail(SWB_E_FLOAT_OUTPUT);
     if (int rc = swb_gate(gate_config, wg, wu, x, bg, bu, h, inter, hidden, 0, stream)) return rc;
-    return swb_project(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream);
+    return project_impl(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream, true);
+}
+
+int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, const void* wu_shard, const void* wd_shard,
+               const void* x, const void* bg_shard, const void* bu_shard, void* h_shard, float* y_partial, int hidden,
+               int shard, void* stream) {
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
+    if (!wd_shard) return fail(SWB_E_INPUT);
+    if (!y_partial) return fail(SWB_E_FLOAT_OUTPUT);
+    if (int rc = swb_gate(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream))
+        return rc;
+    return project_impl(down_config, wd_shard, h_shard, nullptr, nullptr, y_partial, hidden, shard, 0, stream, true);
 }
 
 int swb_swiglu_out(const void* x, const void* gate, const void* up, const void* down, void* h, void* y,
@@ -309,8 +352,8 @@ int swb_swiglu_out(const void* x, const void* gate, const void* up, const void* 
     if (overlaps(h, ib, y, hb)) return fail(SWB_E_OVERLAP_OUTPUT);
     if (int rc = swb_gate(int(gate_config), gate, up, x, nullptr, nullptr, h, int(intermediate), int(hidden), 1, stream))
         return rc;
-    return swb_project(int(down_config), down, h, nullptr, nullptr, y, int(hidden), int(intermediate), SWB_HALF_OUT,
-                       stream);
+    return project_impl(int(down_config), down, h, nullptr, nullptr, y, int(hidden), int(intermediate), SWB_HALF_OUT,
+                        stream, true);
 }
 
 int swb_gate_epilogue(const float* a, const float* b, const void* bg, const void* bu, void* h, int n, void* stream) {

@@ -81,6 +81,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_gate": ([_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
         "swb_project": ([_i, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_uint, _vp], _i),
         "swb_ffn": ([_i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "swb_ffn_tp": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_swiglu_out": ([_vp] * 6 + [_i64] * 4 + [_vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),
         "swb_residual_epilogue": ([_vp, _vp, _vp, _i, _vp], _i),

@@ -141,6 +141,18 @@ def ffn(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, b
                                       y.data_ptr(), hidden, inter, s))
 
 
+def ffn_tp(x: torch.Tensor, wg_shard: torch.Tensor, wu_shard: torch.Tensor, wd_shard: torch.Tensor,
+           bg_shard: torch.Tensor | None, bu_shard: torch.Tensor | None, h_shard: torch.Tensor,
+           y_partial: torch.Tensor, gate_config: int, down_config: int, stream: int | None = None) -> None:
+    """One tensor-parallel rank: h_r = gate(shard rows), y_partial = Wd[:, shard] h_r (fp32, no bias)."""
+    shard, hidden = wg_shard.shape
+    s = _stream(x.device) if stream is None else stream
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().swb_ffn_tp(int(gate_config), int(down_config), wg_shard.data_ptr(),
+                                         wu_shard.data_ptr(), wd_shard.data_ptr(), x.data_ptr(), _ptr(bg_shard),
+                                         _ptr(bu_shard), h_shard.data_ptr(), y_partial.data_ptr(), hidden, shard, s))
+
+
 def residual_epilogue(y: torch.Tensor, bias: torch.Tensor, x: torch.Tensor, stream: int | None = None) -> None:
     """y += bias + x (kernels.cuh:163-166); closes a tensor-parallel layer."""
     s = _stream(y.device) if stream is None else stream

@@ -77,10 +77,21 @@ class ClockSampler:
             self._thread.start()
         return self
 
-    def stop(self) -> dict:
+    def stop(self, window: tuple[float, float] | None = None) -> dict:
+        """Stop sampling; summarise the samples inside `window` (host times bracketing the
+        timed region), or every loaded sample when the window caught fewer than three."""
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=5)
+        if window is not None and self._nvml is not None:
+            inside = [s for s in self.samples if window[0] <= s["t"] <= window[1]]
+            if len(inside) >= 3:
+                out = self.summary(inside)
+                out["window"] = "timed region"
+                return out
+            out = self.summary()
+            out["window"] = f"timed region ({len(inside)} samples) and the loaded phases around it"
+            return out
         return self.summary()
 
     def max_mhz(self):
@@ -91,16 +102,17 @@ class ClockSampler:
         except Exception:
             return None
 
-    def summary(self) -> dict:
+    def summary(self, samples: list[dict] | None = None) -> dict:
         if self._nvml is None:
             return _smi_snapshot(self.index)
-        loaded = [s for s in self.samples if not (s["mask"] & 0x1)] or self.samples
+        samples = self.samples if samples is None else samples
+        loaded = [s for s in samples if not (s["mask"] & 0x1)] or samples
         reasons = sorted({name for s in loaded for bit, name in _REASONS.items() if s["mask"] & bit} - {"gpu_idle"})
         return {
             "sm_mhz": statistics.median(s["sm_mhz"] for s in loaded) if loaded else None,
             "sm_max_mhz": self.max_mhz(),
             "reasons": reasons,
-            "samples": len(self.samples),
+            "samples": len(samples),
             "samples_under_load": len(loaded),
             "power_w_max": max((s["power_w"] for s in loaded if s["power_w"] is not None), default=None),
             "source": "nvml",

@@ -98,6 +98,17 @@ SWB_API int swb_ffn(int gate_config, int down_config, const void* wg, const void
             const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
             void* stream);
 
+/* Tensor-parallel rank of the layer (no counterpart in the reference, which is
+ * single-GPU; it splits benchmark.cu:161-165 n ways). wg_shard, wu_shard: rows
+ * [r*inter/n, (r+1)*inter/n) of Wg, Wu -> [shard, hidden]; wd_shard: the matching
+ * columns of Wd stored contiguously -> [hidden, shard]; bg_shard, bu_shard: [shard]
+ * or NULL; h_shard: [shard] fp16 workspace; y_partial: [hidden] fp32 = Wd_r h_r, no
+ * bias or residual. The caller all-reduces y_partial over the ranks (sum) and then
+ * applies swb_residual_epilogue(y, bd, x) once. */
+SWB_API int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
+                       const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard,
+                       void* h_shard, float* y_partial, int hidden, int shard, void* stream);
+
 /* swiglu_out, src/torch_extension.cu:7-40: the binding's shape / config / alias guards,
  * then the model-rounding gate into h [inter] and the fp16 down projection into
  * y [hidden] (no bias, no residual -- the residual stays in the transformer layer).
