@@ -324,6 +324,18 @@ def ours(args) -> None:
     if world > 1:
         dist.barrier()
     elapsed_ms = start.elapsed_time(end)
+    # A timed region shorter than a few NVML samples is followed by a soak of the same
+    # graph replays (not timed) so the clock record reflects this load.
+    soak_window = None
+    if t_window[1] - t_window[0] < 0.3:
+        soak_steps = int(math.ceil(0.3 / max(t_window[1] - t_window[0], 1e-4) * args.steps))
+        t0 = time.time()
+        for i in range(soak_steps):
+            run_step(i)
+        torch.cuda.synchronize()
+        soak_window = (t0, time.time())
+        if world > 1:
+            dist.barrier()
     if world > 1:
         t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -430,7 +442,7 @@ def ours(args) -> None:
                   "kernels_per_step": 5, "speedup_vs_cublas": res[algo] / us_per_layer}
         base.close()
 
-    clocks = sampler.stop(window=tuple(t_window))
+    clocks = sampler.stop(window=tuple(t_window), fallback_window=soak_window)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(sets, common, H, I, args.cpu_seconds)

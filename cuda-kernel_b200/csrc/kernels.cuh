@@ -41,7 +41,8 @@ struct Params {
     int cols;
     int model_round;
     int x_staged;  // ldg_kernel: x copied to shared memory as fp32
-    int stages;    // bulk_kernel: ring depth
+    int stages;    // bulk_kernel / rbulk_kernel: ring depth
+    int row_stage; // rbulk_kernel: whole rows per ring stage
 };
 
 template <int MODE>
@@ -433,6 +434,177 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
             ch = 0;
             ++row;
         }
+        if (++s == stages) { s = 0; ph ^= 1u; }
+    }
+    named_barrier_sync(1, CT);
+    if (s_failed) return;
+    for (int i = t; i < nrows; i += CT) {
+        float a = 0.f, b = 0.f;
+        for (int j = 0; j < CW; ++j) {
+            a += part[(size_t(i) * CW + j) * NM];
+            if constexpr (GATED) b += part[(size_t(i) * CW + j) * NM + 1];
+        }
+        write_row<MODE>(p, r0 + i, a, b);
+    }
+}
+
+// ===================================================================== RBULK
+
+// Shared-memory layout of rbulk_kernel, shared by host sizing and device code.
+__host__ __device__ inline BulkLayout rbulk_layout(int nm, int row_stage, int cols, int stages, int cw,
+                                                   int rows_per_cta) {
+    BulkLayout L;
+    L.ring = 0;
+    const size_t off = size_t(stages) * row_stage * nm * size_t(cols) * 2;
+    L.full = align_up(off, 16);
+    L.empty = L.full + size_t(stages) * 8;
+    L.xs = align_up(L.empty + size_t(stages) * 8, 16);  // no x copy: x lives in registers
+    L.part = L.xs;
+    L.total = align_up(L.part + size_t(rows_per_cta) * cw * nm * 4, 16);
+    return L;
+}
+
+// Persistent row-stage streaming kernel. CTA b owns rows [b*rows/G, (b+1)*rows/G).
+// A producer thread streams them with one cp.async.bulk per matrix per ring
+// stage; a stage holds `row_stage` whole rows, which are contiguous in a
+// row-major matrix. Consumer thread t owns the 16-byte vectors t + j*CT (j <
+// MAXJ) of EVERY row, so its slice of x is loaded once into registers and the
+// only shared-memory traffic is the weights themselves (written by the copy
+// engine, read once by the consumers). Row sums: a warp reduction per row into
+// a fixed slot, combined across warps in a fixed order at the end.
+template <int CW, int MAXJ, int CPS, int MODE>
+__global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params p) {
+    constexpr bool GATED = MODE == MODE_GATE;
+    constexpr int NM = GATED ? 2 : 1;
+    constexpr int CT = CW * 32;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int s_failed;
+
+    const int G = gridDim.x;
+    const int r0 = int((long long)blockIdx.x * p.rows / G);
+    const int r1 = int((long long)(blockIdx.x + 1) * p.rows / G);
+    const int nrows = r1 - r0;
+    if (nrows <= 0) return;  // whole CTA leaves together
+    const int cols = p.cols;
+    const int nv = cols / 8;
+    const int rs = p.row_stage;
+    const int stages = p.stages;
+    const int units = (nrows + rs - 1) / rs;
+    const int rows_per_cta = (p.rows + G - 1) / G;
+    const size_t stage_halves = size_t(rs) * NM * cols;
+
+    const BulkLayout L = rbulk_layout(NM, rs, cols, stages, CW, rows_per_cta);
+    __half* ring = reinterpret_cast<__half*>(smem + L.ring);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    float* part = reinterpret_cast<float*>(smem + L.part);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        s_failed = 0;
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), CW);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    griddep_launch_dependents();
+
+    if (warp == CW) {
+        // ------------------------------------------------------- producer
+        if (lane != 0) return;
+        const uint64_t pol = l2_evict_first_policy();
+        int s = 0, issued = 0;
+        uint32_t ph = 0;
+        for (int k = 0; k < units; ++k) {
+            if (k >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) break;
+            const int row = r0 + k * rs;
+            const int ru = min(rs, r1 - row);
+            const uint32_t bytes = uint32_t(ru) * uint32_t(cols) * 2u;
+            const uint32_t fb = smem_u32(full + s);
+            mbar_arrive_expect_tx(fb, bytes * NM);
+            const size_t goff = size_t(row) * cols;
+            __half* dst = ring + size_t(s) * stage_halves;
+            bulk_copy_g2s(smem_u32(dst), p.w + goff, bytes, fb, pol);
+            if constexpr (GATED) bulk_copy_g2s(smem_u32(dst + size_t(rs) * cols), p.u + goff, bytes, fb, pol);
+            ++issued;
+            if (++s == stages) { s = 0; ph ^= 1u; }
+        }
+        const int drain = issued < stages ? issued : stages;
+        for (int j = 1; j <= drain; ++j) {
+            const int k = issued - j;
+            if (!mbar_wait(smem_u32(full + (k % stages)), uint32_t((k / stages) & 1))) break;
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    const int t = threadIdx.x;
+    griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
+    float xr[MAXJ][8];
+    const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+#pragma unroll
+    for (int j = 0; j < MAXJ; ++j) {
+        const int v = t + j * CT;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xr[j][e] = 0.f;
+        if (v < nv) {
+            if (x16) {
+                const uint4 q = *reinterpret_cast<const uint4*>(p.x + size_t(v) * 8);
+                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = half2_bits_to_float2(w4[k]);
+                    xr[j][2 * k] = f.x;
+                    xr[j][2 * k + 1] = f.y;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xr[j][e] = __half2float(p.x[size_t(v) * 8 + e]);
+            }
+        }
+    }
+
+    int s = 0;
+    uint32_t ph = 0;
+    for (int k = 0; k < units; ++k) {
+        if (!mbar_wait(smem_u32(full + s), ph)) {
+            s_failed = 1;
+            break;
+        }
+        const int row0 = r0 + k * rs;
+        const int ru = min(rs, r1 - row0);
+        const __half* sw = ring + size_t(s) * stage_halves;
+        for (int r = 0; r < ru; ++r) {
+            float acc[NM][4];
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
+            const __half* wrow = sw + size_t(r) * cols;
+#pragma unroll
+            for (int j = 0; j < MAXJ; ++j) {
+                const int v = t + j * CT;
+                if (v < nv) {
+                    dot8(*reinterpret_cast<const uint4*>(wrow + size_t(v) * 8), xr[j], acc[0]);
+                    if constexpr (GATED)
+                        dot8(*reinterpret_cast<const uint4*>(wrow + size_t(rs) * cols + size_t(v) * 8), xr[j],
+                             acc[1]);
+                }
+            }
+            const float a = warp_sum(fold4(acc[0]));
+            float b = 0.f;
+            if constexpr (GATED) b = warp_sum(fold4(acc[1]));
+            if (lane == 0) {
+                const size_t slot = (size_t(row0 - r0 + r) * CW + warp) * NM;
+                part[slot] = a;
+                if constexpr (GATED) part[slot + 1] = b;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(empty + s));
         if (++s == stages) { s = 0; ph ^= 1u; }
     }
     named_barrier_sync(1, CT);

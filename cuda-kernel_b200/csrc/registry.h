@@ -16,10 +16,18 @@
 //   (the launcher trims it to the shared memory the shape leaves free).
 //   A BULK id whose preconditions fail for a shape (cols % 8, 16-byte rows,
 //   shared-memory fit) runs the LDG geometry of id 33 instead.
+// RBULK family (persistent, whole rows per ring stage, x held in registers):
+//   warps  = consumer warps (plus one producer warp), rows = CTAs per SM,
+//   unroll = MAXJ, the 16-byte vectors of a row each consumer thread owns
+//            (so cols <= 8 * 32 * warps * unroll),
+//   chunk  = target bytes per ring stage (whole rows, at least one),
+//   stages = maximum ring depth (trimmed to the shared memory available).
+//   An RBULK id whose preconditions fail runs the BULK geometry of id 64.
 #pragma once
 
 #define SWB_FAM_LDG 0
 #define SWB_FAM_BULK 1
+#define SWB_FAM_RBULK 2
 
 #define SWB_CONFIGS(X)                                                                          \
     X(1, SWB_FAM_LDG, 1, 4, 2, 1, 0, 0)                                                         \
@@ -44,7 +52,17 @@
     X(66, SWB_FAM_BULK, 4, 1, 8, 1, 4096, 8)                                                    \
     X(67, SWB_FAM_BULK, 16, 1, 8, 1, 8192, 4)                                                   \
     X(68, SWB_FAM_BULK, 8, 2, 8, 1, 2048, 8)                                                    \
-    X(69, SWB_FAM_BULK, 4, 2, 8, 1, 4096, 4)
+    X(69, SWB_FAM_BULK, 4, 2, 8, 1, 4096, 4)                                                    \
+    X(80, SWB_FAM_RBULK, 4, 2, 8, 4, 16384, 8)                                                  \
+    X(81, SWB_FAM_RBULK, 8, 1, 8, 4, 32768, 8)                                                  \
+    X(82, SWB_FAM_RBULK, 16, 1, 8, 4, 32768, 8)                                                 \
+    X(83, SWB_FAM_RBULK, 8, 2, 8, 4, 16384, 8)                                                  \
+    X(85, SWB_FAM_RBULK, 8, 1, 8, 8, 32768, 8)                                                  \
+    X(86, SWB_FAM_RBULK, 4, 2, 8, 8, 16384, 8)                                                  \
+    X(87, SWB_FAM_RBULK, 8, 2, 8, 8, 16384, 6)                                                  \
+    X(88, SWB_FAM_RBULK, 4, 1, 8, 4, 16384, 16)                                                 \
+    X(89, SWB_FAM_RBULK, 4, 1, 8, 8, 32768, 12)
 
-// Id used when a BULK geometry cannot run a shape.
+// Ids used when a BULK / RBULK geometry cannot run a shape.
 #define SWB_BULK_FALLBACK_ID 33
+#define SWB_RBULK_FALLBACK_ID 64

@@ -57,7 +57,9 @@ const swb_config_t* find_config(int64_t id) {
     static_assert(FAM != SWB_FAM_LDG || PK == 2 || PK == 8, "LDG pack");                            \
     static_assert(FAM != SWB_FAM_LDG || U == 1 || U == 2 || U == 4 || U == 8, "LDG unroll");        \
     static_assert(FAM != SWB_FAM_BULK || (CH % 8 == 0 && CH > 0 && ST >= 2 && (W + 1) * 32 <= 1024), \
-                  "BULK geometry");
+                  "BULK geometry");                                                                \
+    static_assert(FAM != SWB_FAM_RBULK || (U >= 1 && U <= 8 && CH >= 16 && ST >= 2 && (W + 1) * 32 <= 1024), \
+                  "RBULK geometry");
 SWB_CONFIGS(SWB_CHECK)
 #undef SWB_CHECK
 
@@ -144,6 +146,9 @@ int launch_bulk(Params p, cudaStream_t stream, bool pdl);
 template <int MODE>
 int run_fallback(Params p, cudaStream_t stream, bool pdl);
 
+template <int MODE>
+int dispatch_fallback(int64_t id, Params p, cudaStream_t stream, bool pdl);
+
 template <int FAM, int W, int R, int PK, int U, int CH, int ST>
 struct Launcher;
 
@@ -186,6 +191,45 @@ int launch_bulk(Params p, cudaStream_t stream, bool pdl) {
     return check_launch();
 }
 
+template <int CW, int CPS, int MAXJ, int STAGE_BYTES, int ST, int MODE>
+int launch_rbulk(Params p, cudaStream_t stream, bool pdl) {
+    constexpr int NM = MODE == MODE_GATE ? 2 : 1;
+    static std::atomic<uint64_t> smem_set{0};
+    const int nv = p.cols / 8;
+    const bool ok = (p.cols % 8) == 0 && (reinterpret_cast<uintptr_t>(p.w) % 16) == 0 &&
+                    (NM == 1 || (reinterpret_cast<uintptr_t>(p.u) % 16) == 0) && nv <= MAXJ * CW * 32;
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const int G = std::min(sms * CPS, p.rows);
+    const int rows_per_cta = (p.rows + G - 1) / G;
+    const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 64;
+    const size_t row_bytes = size_t(NM) * p.cols * 2;
+    int rs = int(std::max<size_t>(1, STAGE_BYTES / std::max<size_t>(row_bytes, 1)));
+    rs = std::min(rs, rows_per_cta);
+    int stages = 0;
+    for (; rs >= 1; rs = rs > 1 ? rs / 2 : 0) {  // shrink the stage until at least two fit
+        stages = ST;
+        while (stages >= 2 && rbulk_layout(NM, rs, p.cols, stages, CW, rows_per_cta).total > budget) --stages;
+        if (stages >= 2 || rs == 1) break;
+    }
+    if (!ok || rs < 1 || stages < 2) return dispatch_fallback<MODE>(SWB_RBULK_FALLBACK_ID, p, stream, pdl);
+    p.stages = stages;
+    p.row_stage = rs;
+    const size_t smem = rbulk_layout(NM, rs, p.cols, stages, CW, rows_per_cta).total;
+    auto kernel = rbulk_kernel<CW, MAXJ, CPS, MODE>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    launch_kernel(kernel, unsigned(G), (CW + 1) * 32, smem, stream, pdl, p);
+    return check_launch();
+}
+
+template <int W, int R, int PK, int U, int CH, int ST>
+struct Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST> {
+    template <int MODE>
+    static int run(Params p, cudaStream_t s, bool pdl) {
+        return launch_rbulk<W, R, U, CH, ST, MODE>(p, s, pdl);
+    }
+};
+
 template <int MODE>
 int dispatch(int64_t id, const Params& p, cudaStream_t s, bool pdl = false) {
     switch (id) {
@@ -202,6 +246,11 @@ int dispatch(int64_t id, const Params& p, cudaStream_t s, bool pdl = false) {
 template <int MODE>
 int run_fallback(Params p, cudaStream_t stream, bool pdl) {
     return dispatch<MODE>(SWB_BULK_FALLBACK_ID, p, stream, pdl);
+}
+
+template <int MODE>
+int dispatch_fallback(int64_t id, Params p, cudaStream_t stream, bool pdl) {
+    return dispatch<MODE>(id, p, stream, pdl);
 }
 
 bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {

@@ -57,11 +57,7 @@ class ClockSampler:
             power = n.nvmlDeviceGetPowerUsage(h) / 1000.0
         except Exception:
             power = None
-        try:
-            util = n.nvmlDeviceGetUtilizationRates(h).gpu
-        except Exception:
-            util = None
-        return {"t": time.time(), "sm_mhz": sm, "mask": int(mask), "power_w": power, "util": util}
+        return {"t": time.time(), "sm_mhz": sm, "mask": int(mask), "power_w": power}
 
     def _run(self):
         while not self._stop.is_set():
@@ -77,20 +73,23 @@ class ClockSampler:
             self._thread.start()
         return self
 
-    def stop(self, window: tuple[float, float] | None = None) -> dict:
+    def stop(self, window: tuple[float, float] | None = None,
+             fallback_window: tuple[float, float] | None = None) -> dict:
         """Stop sampling; summarise the samples inside `window` (host times bracketing the
-        timed region), or every loaded sample when the window caught fewer than three."""
+        timed region). When it caught fewer than three, add those of `fallback_window`
+        (an untimed soak of the same work right after it)."""
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=5)
         if window is not None and self._nvml is not None:
             inside = [s for s in self.samples if window[0] <= s["t"] <= window[1]]
-            if len(inside) >= 3:
-                out = self.summary(inside)
-                out["window"] = "timed region"
+            if len(inside) >= 3 or fallback_window is None:
+                out = self.summary(inside or self.samples)
+                out["window"] = "timed region" if inside else "whole run"
                 return out
-            out = self.summary()
-            out["window"] = f"timed region ({len(inside)} samples) and the loaded phases around it"
+            soak = [s for s in self.samples if fallback_window[0] <= s["t"] <= fallback_window[1]]
+            out = self.summary(inside + soak)
+            out["window"] = f"timed region ({len(inside)} samples) + untimed soak of the same graphs ({len(soak)})"
             return out
         return self.summary()
 

@@ -50,6 +50,7 @@ extern "C" {
 /* kernel families in the registry */
 #define SWB_FAMILY_LDG 0  /* register-streaming 128/32-bit loads, x staged in shared memory */
 #define SWB_FAMILY_BULK 1 /* persistent: cp.async.bulk ring + mbarriers, one producer warp */
+#define SWB_FAMILY_RBULK 2 /* persistent: whole-row ring stages, x held in registers */
 
 /* Host metadata of one launch geometry (include/config.hpp:5 struct Config). */
 typedef struct swb_config {
@@ -58,9 +59,9 @@ typedef struct swb_config {
     int warps;   /* LDG: warps per output row. BULK: consumer warps per CTA */
     int rows;    /* LDG: rows per CTA. BULK: CTAs per SM */
     int pack;    /* halves per vector load (2 = 32-bit, 8 = 128-bit) */
-    int unroll;  /* LDG: independent vector loads in flight per matrix per thread */
-    int chunk;   /* BULK: halves per matrix per pipeline stage (0 for LDG) */
-    int stages;  /* BULK: maximum ring depth (0 for LDG) */
+    int unroll;  /* LDG: vector loads in flight per matrix per thread. RBULK: vectors of a row per thread */
+    int chunk;   /* BULK: halves per matrix per stage. RBULK: target bytes per stage. 0 for LDG */
+    int stages;  /* BULK, RBULK: maximum ring depth (0 for LDG) */
 } swb_config_t;
 
 SWB_API const char* swb_status_string(int status);

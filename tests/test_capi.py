@@ -65,9 +65,11 @@ def test_registry_keeps_reference_ids_and_rejects_invalid():
         if c["family"] == _lib.SWB_FAMILY_LDG:
             assert c["warps"] * c["rows"] * 32 <= 1024 and c["pack"] in (2, 8)
             assert c["chunk"] == 0 and c["stages"] == 0
-        else:
-            assert c["family"] == _lib.SWB_FAMILY_BULK
+        elif c["family"] == _lib.SWB_FAMILY_BULK:
             assert c["chunk"] % 8 == 0 and c["stages"] >= 2 and (c["warps"] + 1) * 32 <= 1024
+        else:
+            assert c["family"] == _lib.SWB_FAMILY_RBULK
+            assert 1 <= c["unroll"] <= 8 and c["stages"] >= 2 and (c["warps"] + 1) * 32 <= 1024
         if cid in ref_geom:
             assert (c["warps"], c["rows"], c["pack"]) == ref_geom[cid]
     with pytest.raises(RuntimeError, match="unknown kernel configuration"):

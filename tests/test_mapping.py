@@ -169,6 +169,79 @@ def audit_bulk(cfg, rows, cols, gated):
     return True
 
 
+def rbulk_layout(nm, rs, cols, stages, cw, rows_per_cta):
+    def up(v, a):
+        return (v + a - 1) // a * a
+    full = up(stages * rs * nm * cols * 2, 16)
+    empty = full + stages * 8
+    part = up(empty + stages * 8, 16)
+    return {"full": full, "empty": empty, "part": part, "total": up(part + rows_per_cta * cw * nm * 4, 16)}
+
+
+def rbulk_plan(cfg, rows, cols, gated, w_aligned=True):
+    """Mirror of launch_rbulk: None when the fallback geometry runs."""
+    nm = 2 if gated else 1
+    cw, cps, maxj, target, smax = cfg["warps"], cfg["rows"], cfg["unroll"], cfg["chunk"], cfg["stages"]
+    nv = cols // 8
+    ok = cols % 8 == 0 and w_aligned and nv <= maxj * cw * 32
+    G = min(SMS * cps, rows)
+    rpc = (rows + G - 1) // G
+    budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 64
+    row_bytes = nm * cols * 2
+    rs = min(max(1, target // max(row_bytes, 1)), rpc)
+    stages = 0
+    while rs >= 1:
+        stages = smax
+        while stages >= 2 and rbulk_layout(nm, rs, cols, stages, cw, rpc)["total"] > budget:
+            stages -= 1
+        if stages >= 2 or rs == 1:
+            break
+        rs = rs // 2 if rs > 1 else 0
+    if not ok or rs < 1 or stages < 2:
+        return None
+    return {"G": G, "rpc": rpc, "rs": rs, "stages": stages, "budget": budget,
+            "layout": rbulk_layout(nm, rs, cols, stages, cw, rpc)}
+
+
+def audit_rbulk(cfg, rows, cols, gated):
+    plan = rbulk_plan(cfg, rows, cols, gated)
+    if plan is None:
+        return False
+    nm = 2 if gated else 1
+    CT = cfg["warps"] * 32
+    nv = cols // 8
+    G, rs, stages, L = plan["G"], plan["rs"], plan["stages"], plan["layout"]
+    assert L["total"] <= plan["budget"] and L["full"] % 16 == 0 and L["part"] % 16 == 0
+    # consumer ownership of a row's vectors: t + j*CT for j < MAXJ covers [0, nv) once
+    counts = np.zeros(nv, np.int64)
+    for t in range(CT):
+        for j in range(cfg["unroll"]):
+            v = t + j * CT
+            if v < nv:
+                counts[v] += 1
+    assert (counts == 1).all()
+    owner = np.zeros(rows, np.int64)
+    stage_bytes = rs * nm * cols * 2
+    for b in range(G):
+        r0, r1 = (b * rows) // G, ((b + 1) * rows) // G
+        assert 1 <= r1 - r0 <= plan["rpc"]
+        units = (r1 - r0 + rs - 1) // rs
+        covered = 0
+        for k in range(units):
+            s = k % stages
+            row = r0 + k * rs
+            ru = min(rs, r1 - row)
+            nbytes = ru * cols * 2
+            assert nbytes % 16 == 0 and (2 * row * cols) % 16 == 0
+            assert s * stage_bytes % 16 == 0 and s * stage_bytes + nm * rs * cols * 2 <= L["full"]
+            assert nbytes * nm < (1 << 20)
+            owner[row:row + ru] += 1
+            covered += ru
+        assert covered == r1 - r0
+    assert (owner == 1).all()
+    return True
+
+
 @pytest.fixture(scope="module")
 def configs():
     return [config_info(i) for i in config_ids()]
@@ -219,3 +292,25 @@ def test_bulk_falls_back_when_unaligned(configs):
         if cfg["family"] == 1:
             assert bulk_plan(cfg, 5631, 2047, True) is None
             assert bulk_plan(cfg, 64, 64, True, w_aligned=False) is None
+
+
+@pytest.mark.parametrize("shape", CORRECTNESS + EXTRA + [(4096, 1792), (4096, 2752), (4096, 1376)])
+def test_rbulk_plan_and_coverage(configs, shape):
+    h, i = shape
+    ran = 0
+    for cfg in configs:
+        if cfg["family"] != 2:
+            continue
+        for rows, cols, gated in ((i, h, True), (h, i, False)):
+            ran += audit_rbulk(cfg, rows, cols, gated)
+    if h % 8 == 0 and i % 8 == 0 and max(h, i) <= 8192:
+        assert ran > 0
+
+
+def test_rbulk_covers_the_layer_shapes(configs):
+    """Some RBULK geometry runs every gate and down shape of the benchmarked layers (and TP shards)."""
+    for rows, cols, gated in ((14336, 4096, True), (4096, 14336, False), (11008, 4096, True),
+                              (4096, 11008, False), (5632, 2048, True), (2048, 5632, False),
+                              (1792, 4096, True), (4096, 1792, False), (7168, 4096, True), (4096, 7168, False)):
+        plans = [rbulk_plan(c, rows, cols, gated) for c in configs if c["family"] == 2]
+        assert any(p is not None for p in plans), (rows, cols)
