@@ -288,6 +288,7 @@ const char* swb_status_string(int status) {
         case SWB_E_CUDA: return "CUDA error";
         case SWB_E_DEVICE: return "device-side error";
         case SWB_E_UNSUPPORTED: return "unsupported device";
+        case SWB_E_WORKSPACE: return "intermediate size exceeds the built-in workspace";
         default: return "unknown status";
     }
 }
@@ -433,3 +434,47 @@ int swb_device_error(int clear, int* out) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// swb_ffn_noalloc: the layer for callers that cannot allocate device memory.
+// h lives in this fixed array (one copy per device that loads the library).
+// Host code must not hand `g_noalloc_h` to a kernel directly -- on the host the
+// name is only a stand-in; its device address is looked up per device below.
+namespace {
+
+static __device__ __align__(256) __half g_noalloc_h[SWB_NOALLOC_MAX_INTER];
+
+std::atomic<void*> g_noalloc_ptr[64];
+
+// Device address of g_noalloc_h on the current device, looked up once per device.
+int noalloc_workspace(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return fail(SWB_E_UNSUPPORTED, "device index beyond 63");
+    void* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        e = cudaGetSymbolAddress(&p, g_noalloc_h);
+        if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+        if (!p) return fail(SWB_E_CUDA, "no device address for the built-in workspace");
+        g_noalloc_ptr[dev].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return SWB_OK;
+}
+
+}  // namespace
+
+extern "C" int swb_ffn_noalloc(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
+                               const void* x, const void* bg, const void* bu, const void* bd, float* y, int hidden,
+                               int inter, void* stream) {
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
+    if (hidden <= 0 || inter <= 0 || !wg || !x || !wd) return fail(SWB_E_INPUT);
+    if (!wu) return fail(SWB_E_GATE_BUFFERS);
+    if (!y) return fail(SWB_E_FLOAT_OUTPUT);
+    if (inter > SWB_NOALLOC_MAX_INTER)
+        return fail(SWB_E_WORKSPACE, "swb_ffn_noalloc holds at most 65536 intermediate values");
+    void* h = nullptr;
+    if (int rc = noalloc_workspace(&h)) return rc;
+    return swb_ffn(gate_config, down_config, wg, wu, wd, x, bg, bu, bd, h, y, hidden, inter, stream);
+}

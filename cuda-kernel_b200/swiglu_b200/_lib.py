@@ -35,6 +35,8 @@ SWB_E_OVERLAP_OUTPUT = 11
 SWB_E_CUDA = 12
 SWB_E_DEVICE = 13
 SWB_E_UNSUPPORTED = 14
+SWB_E_WORKSPACE = 15
+SWB_NOALLOC_MAX_INTER = 65536
 SWB_RESIDUAL = 1
 SWB_HALF_OUT = 2
 SWB_FAMILY_LDG = 0
@@ -83,6 +85,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_project": ([_i, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_uint, _vp], _i),
         "swb_ffn": ([_i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
         "swb_ffn_tp": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
+        "swb_ffn_noalloc": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_swiglu_out": ([_vp] * 6 + [_i64] * 4 + [_vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),
         "swb_residual_epilogue": ([_vp, _vp, _vp, _i, _vp], _i),

@@ -42,6 +42,7 @@ extern "C" {
 #define SWB_E_CUDA 12          /* CUDA runtime error; detail in swb_last_error() */
 #define SWB_E_DEVICE 13        /* a kernel gave up a bounded wait (device error word set) */
 #define SWB_E_UNSUPPORTED 14   /* no usable sm_100 device / feature */
+#define SWB_E_WORKSPACE 15     /* size beyond the built-in workspace of swb_ffn_noalloc */
 
 /* project() flags (template flags of decode::launch, include/kernels.cuh:136) */
 #define SWB_RESIDUAL 1u /* add residual[row] after bias (RESIDUAL) */
@@ -98,6 +99,26 @@ SWB_API int swb_project(int config, const void* w, const void* x, const void* bi
 SWB_API int swb_ffn(int gate_config, int down_config, const void* wg, const void* wu, const void* wd, const void* x,
             const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
             void* stream);
+
+/* swb_ffn without a workspace argument. No counterpart in the reference.
+ * Some callers cannot allocate device memory at all: code that only receives
+ * raw pointers through a foreign-function boundary with no allocator bound,
+ * serving runtimes that hand every byte of device memory to their own pool
+ * up front, and latency-critical loops that must never hit an allocation
+ * (which may synchronise the device). For them, h lives in a fixed array inside
+ * this library (SWB_NOALLOC_MAX_INTER halves = 128 KiB, held by every GPU that
+ * loads the library until the process exits); the caller still passes inputs
+ * and y. Nothing is allocated: no cudaMalloc/cudaFree and no library routine
+ * that allocates. inter > SWB_NOALLOC_MAX_INTER returns SWB_E_WORKSPACE.
+ * The first call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress) -- make it before any stream capture on that device.
+ * Every call shares the one array: h is fully rewritten by each call, so nothing
+ * needs clearing, but calls that may overlap on the GPU (other streams, other
+ * threads) race on it and must be serialised by the caller. */
+#define SWB_NOALLOC_MAX_INTER 65536
+SWB_API int swb_ffn_noalloc(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
+                            const void* x, const void* bg, const void* bu, const void* bd, float* y, int hidden,
+                            int inter, void* stream);
 
 /* Tensor-parallel rank of the layer (no counterpart in the reference, which is
  * single-GPU; it splits benchmark.cu:161-165 n ways). wg_shard, wu_shard: rows
