@@ -124,6 +124,39 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ---------------------------------------------------- cluster launch control
+// Work stealing on sm_100: try_cancel asks the hardware to cancel a CTA of this
+// grid that has not started yet and writes a 16-byte response into shared memory,
+// completing `bar` with 16 transaction bytes. The response says whether a CTA was
+// cancelled and, if so, its blockIdx -- whose work the caller then does itself.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+    asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];"
+                 ::"r"(resp), "r"(bar) : "memory");
+}
+
+// Orders generic-proxy accesses to shared memory against async-proxy ones.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Decodes a try_cancel response: returns the cancelled CTA's x index, or -1 when
+// no CTA was left to cancel.
+__device__ __forceinline__ int clc_decode(const uint4& r) {
+    const unsigned long long lo = (unsigned long long)r.x | ((unsigned long long)r.y << 32);
+    const unsigned long long hi = (unsigned long long)r.z | ((unsigned long long)r.w << 32);
+    uint32_t ok, x;
+    asm volatile(
+        "{\n\t.reg .b128 rr;\n\t.reg .pred p;\n\t"
+        "mov.b128 rr, {%2, %3};\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, rr;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, rr;\n\t}"
+        : "=r"(ok), "=r"(x)
+        : "l"(lo), "l"(hi)
+        : "memory");
+    return ok ? int(x) : -1;
+}
+
 // Named barrier among the first `threads` threads of the CTA (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -42,7 +42,8 @@ struct Params {
     int model_round;
     int x_staged;  // ldg_kernel: x copied to shared memory as fp32
     int stages;    // bulk_kernel / rbulk_kernel: ring depth
-    int row_stage; // rbulk_kernel: whole rows per ring stage
+    int row_stage; // rbulk_kernel / sbulk_kernel: whole rows per ring stage
+    int rows_per_block;  // sbulk_kernel: rows per CTA index (unit of work stealing)
 };
 
 template <int MODE>
@@ -617,6 +618,253 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
         }
         write_row<MODE>(p, r0 + i, a, b);
     }
+}
+
+// ===================================================================== SBULK
+
+// Shared-memory layout of sbulk_kernel (host sizing and device code).
+struct StealLayout {
+    size_t ring, full, empty, meta, cnt, part, total;
+};
+
+__host__ __device__ inline StealLayout sbulk_layout(int nm, int row_stage, int cols, int stages, int cw) {
+    StealLayout L;
+    L.ring = 0;
+    L.full = align_up(size_t(stages) * row_stage * nm * size_t(cols) * 2, 16);
+    L.empty = L.full + size_t(stages) * 8;
+    L.meta = L.empty + size_t(stages) * 8;              // int2 {first row, rows} per stage
+    L.cnt = L.meta + size_t(stages) * 8;                // consumer warps done per stage
+    L.part = align_up(L.cnt + size_t(stages) * 4, 16);  // [stage][row][warp][matrix] partial sums
+    L.total = align_up(L.part + size_t(stages) * row_stage * cw * nm * 4, 16);
+    return L;
+}
+
+// Row-stage streaming with hardware work stealing. The grid has one CTA per
+// block of `rows_per_block` rows; the CTAs that fit run, and each one's producer,
+// while streaming its current block, asks cluster launch control for a CTA that
+// has not started and takes over that CTA's block. Faster SMs therefore take more
+// blocks and the CTAs finish together. A ring stage holds up to `row_stage`
+// whole rows; the producer tags each stage with its rows (or -1 to stop). As in
+// rbulk_kernel, consumer thread t owns vectors t + j*CT of every row, x stays in
+// registers. The last consumer warp to finish a stage sums the stage's row
+// partials over the warps in a fixed order and writes those rows, so outputs are
+// deterministic whatever the stealing order.
+template <int CW, int MAXJ, int CPS, int MODE>
+__global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params p) {
+    constexpr bool GATED = MODE == MODE_GATE;
+    constexpr int NM = GATED ? 2 : 1;
+    constexpr int CT = CW * 32;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(16) uint4 clc_resp[2];
+    __shared__ uint64_t clc_bar[2];
+    __shared__ int s_failed;
+
+    const int cols = p.cols;
+    const int nv = cols / 8;
+    const int rs = p.row_stage;
+    const int rpb = p.rows_per_block;
+    const int stages = p.stages;
+    const size_t stage_halves = size_t(rs) * NM * cols;
+
+    const StealLayout L = sbulk_layout(NM, rs, cols, stages, CW);
+    __half* ring = reinterpret_cast<__half*>(smem + L.ring);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    int2* meta = reinterpret_cast<int2*>(smem + L.meta);
+    int* cnt = reinterpret_cast<int*>(smem + L.cnt);
+    float* part = reinterpret_cast<float*>(smem + L.part);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        s_failed = 0;
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), CW);
+            cnt[s] = 0;
+        }
+        mbar_init(smem_u32(&clc_bar[0]), 1);
+        mbar_init(smem_u32(&clc_bar[1]), 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    griddep_launch_dependents();
+
+    if (warp == CW) {
+        // ------------------------------------------------------- producer
+        if (lane != 0) return;
+        const uint64_t pol = l2_evict_first_policy();
+        int s = 0, issued = 0;
+        uint32_t ph = 0;
+        // Two steal requests stay in flight (slots 0 and 1, answered in the order
+        // issued), so an answer is ready when a block ends. After an answer says
+        // nothing was left, no new request is issued; an older outstanding one is
+        // still collected and, if it did cancel a CTA, that CTA's block is done here.
+        uint32_t clc_ph = 0u;  // bit k: parity of slot k's next answer
+        int q_head = 0, q_len = 0;
+        bool steal_failed = false;
+        auto request = [&](int slot) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(smem_u32(&clc_bar[slot]), 16);
+            clc_try_cancel(smem_u32(&clc_resp[slot]), smem_u32(&clc_bar[slot]));
+        };
+        request(0);
+        request(1);
+        q_len = 2;
+        int block = blockIdx.x;
+        bool ok = true;
+        while (block >= 0 && ok) {
+            const int b0 = block * rpb;
+            const int b1 = min(b0 + rpb, p.rows);
+            for (int row = b0; row < b1; row += rs) {
+                if (issued >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) { ok = false; break; }
+                const int ru = min(rs, b1 - row);
+                const uint32_t bytes = uint32_t(ru) * uint32_t(cols) * 2u;
+                meta[s] = make_int2(row, ru);
+                const uint32_t fb = smem_u32(full + s);
+                mbar_arrive_expect_tx(fb, bytes * NM);
+                const size_t goff = size_t(row) * cols;
+                __half* dst = ring + size_t(s) * stage_halves;
+                bulk_copy_g2s(smem_u32(dst), p.w + goff, bytes, fb, pol);
+                if constexpr (GATED) bulk_copy_g2s(smem_u32(dst + size_t(rs) * cols), p.u + goff, bytes, fb, pol);
+                ++issued;
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+            // Next block: the oldest outstanding answer that cancelled a CTA.
+            block = -1;
+            while (q_len > 0) {
+                const int slot = q_head;
+                if (!mbar_wait(smem_u32(&clc_bar[slot]), (clc_ph >> slot) & 1u)) {
+                    ok = false;  // give this slot up; still try to collect the other one
+                    q_head ^= 1;
+                    --q_len;
+                    continue;
+                }
+                clc_ph ^= 1u << slot;
+                fence_proxy_async_smem();
+                const int nb = clc_decode(clc_resp[slot]);
+                q_head ^= 1;
+                --q_len;
+                if (nb < 0) { steal_failed = true; continue; }
+                if (!steal_failed && ok) { request(slot); ++q_len; }
+                block = nb;
+                break;
+            }
+        }
+        // Collect any request still outstanding (its answer is written asynchronously).
+        while (q_len > 0) {
+            const int slot = q_head;
+            if (mbar_wait(smem_u32(&clc_bar[slot]), (clc_ph >> slot) & 1u)) clc_ph ^= 1u << slot;
+            else ok = false;
+            q_head ^= 1;
+            --q_len;
+        }
+        // Normal end: tag the next stage -1 and complete it without data; the
+        // consumers take every filled stage, in order, before they reach it, so
+        // no copy is in flight when the CTA exits.
+        if (ok && (issued < stages || mbar_wait(smem_u32(empty + s), ph ^ 1u))) {
+            meta[s] = make_int2(-1, 0);
+            mbar_arrive(smem_u32(full + s));
+            return;
+        }
+        // A wait gave up: never leave with copies in flight -- wait (bounded) for
+        // the last fills. (Only here: after the -1 tag above their phases would
+        // no longer be the most recent ones.)
+        const int drain = issued < stages ? issued : stages;
+        for (int j = 1; j <= drain; ++j) {
+            const int k = issued - j;
+            if (!mbar_wait(smem_u32(full + (k % stages)), uint32_t((k / stages) & 1))) break;
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    const int t = threadIdx.x;
+    griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
+    float xr[MAXJ][8];
+    const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+#pragma unroll
+    for (int j = 0; j < MAXJ; ++j) {
+        const int v = t + j * CT;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xr[j][e] = 0.f;
+        if (v < nv) {
+            if (x16) {
+                const uint4 q = *reinterpret_cast<const uint4*>(p.x + size_t(v) * 8);
+                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = half2_bits_to_float2(w4[k]);
+                    xr[j][2 * k] = f.x;
+                    xr[j][2 * k + 1] = f.y;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xr[j][e] = __half2float(p.x[size_t(v) * 8 + e]);
+            }
+        }
+    }
+
+    int s = 0;
+    uint32_t ph = 0;
+    while (true) {
+        if (!mbar_wait(smem_u32(full + s), ph)) {
+            s_failed = 1;
+            break;
+        }
+        const int2 m = meta[s];
+        if (m.x < 0) break;
+        const __half* sw = ring + size_t(s) * stage_halves;
+        float* ps = part + size_t(s) * rs * CW * NM;
+        for (int r = 0; r < m.y; ++r) {
+            float acc[NM][4];
+#pragma unroll
+            for (int mm = 0; mm < NM; ++mm)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[mm][q] = 0.f;
+            const __half* wrow = sw + size_t(r) * cols;
+#pragma unroll
+            for (int j = 0; j < MAXJ; ++j) {
+                const int v = t + j * CT;
+                if (v < nv) {
+                    dot8(*reinterpret_cast<const uint4*>(wrow + size_t(v) * 8), xr[j], acc[0]);
+                    if constexpr (GATED)
+                        dot8(*reinterpret_cast<const uint4*>(wrow + size_t(rs) * cols + size_t(v) * 8), xr[j],
+                             acc[1]);
+                }
+            }
+            const float a = warp_sum(fold4(acc[0]));
+            float b = 0.f;
+            if constexpr (GATED) b = warp_sum(fold4(acc[1]));
+            if (lane == 0) {
+                ps[(size_t(r) * CW + warp) * NM] = a;
+                if constexpr (GATED) ps[(size_t(r) * CW + warp) * NM + 1] = b;
+            }
+        }
+        // The last warp to finish this stage combines the warps' partials and writes the rows.
+        int done = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            done = atomicAdd(cnt + s, 1);
+        }
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done == CW - 1) {
+            __threadfence_block();
+            for (int r = lane; r < m.y; r += 32) {
+                float a = 0.f, b = 0.f;
+                for (int j = 0; j < CW; ++j) {
+                    a += ps[(size_t(r) * CW + j) * NM];
+                    if constexpr (GATED) b += ps[(size_t(r) * CW + j) * NM + 1];
+                }
+                write_row<MODE>(p, m.x + r, a, b);
+            }
+            if (lane == 0) cnt[s] = 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        if (++s == stages) { s = 0; ph ^= 1u; }
+    }
+    (void)s_failed;
 }
 
 // ============================================================== pointwise

@@ -23,11 +23,16 @@
 //   chunk  = target bytes per ring stage (whole rows, at least one),
 //   stages = maximum ring depth (trimmed to the shared memory available).
 //   An RBULK id whose preconditions fail runs the BULK geometry of id 64.
+// SBULK family (RBULK with hardware work stealing): same fields as RBULK; the
+//   grid has one CTA per small block of rows and running CTAs take over blocks
+//   whose CTAs have not started (cluster launch control), so SMs that stream
+//   faster do more of the matrix. Falls back to id 64 like RBULK.
 #pragma once
 
 #define SWB_FAM_LDG 0
 #define SWB_FAM_BULK 1
 #define SWB_FAM_RBULK 2
+#define SWB_FAM_SBULK 3
 
 #define SWB_CONFIGS(X)                                                                          \
     X(1, SWB_FAM_LDG, 1, 4, 2, 1, 0, 0)                                                         \
@@ -53,6 +58,8 @@
     X(67, SWB_FAM_BULK, 16, 1, 8, 1, 8192, 4)                                                   \
     X(68, SWB_FAM_BULK, 8, 2, 8, 1, 2048, 8)                                                    \
     X(69, SWB_FAM_BULK, 4, 2, 8, 1, 4096, 4)                                                    \
+    X(78, SWB_FAM_RBULK, 2, 4, 8, 8, 16384, 3)                                                  \
+    X(79, SWB_FAM_RBULK, 4, 3, 8, 4, 16384, 4)                                                  \
     X(80, SWB_FAM_RBULK, 4, 2, 8, 4, 16384, 8)                                                  \
     X(81, SWB_FAM_RBULK, 8, 1, 8, 4, 32768, 8)                                                  \
     X(82, SWB_FAM_RBULK, 16, 1, 8, 4, 32768, 8)                                                 \
@@ -61,7 +68,17 @@
     X(86, SWB_FAM_RBULK, 4, 2, 8, 8, 16384, 8)                                                  \
     X(87, SWB_FAM_RBULK, 8, 2, 8, 8, 16384, 6)                                                  \
     X(88, SWB_FAM_RBULK, 4, 1, 8, 4, 16384, 16)                                                 \
-    X(89, SWB_FAM_RBULK, 4, 1, 8, 8, 32768, 12)
+    X(89, SWB_FAM_RBULK, 4, 1, 8, 8, 32768, 12)                                                 \
+    X(90, SWB_FAM_SBULK, 4, 2, 8, 4, 16384, 8)                                                  \
+    X(91, SWB_FAM_SBULK, 8, 1, 8, 4, 32768, 8)                                                  \
+    X(92, SWB_FAM_SBULK, 8, 2, 8, 8, 16384, 6)                                                  \
+    X(93, SWB_FAM_SBULK, 16, 1, 8, 4, 32768, 8)                                                 \
+    X(94, SWB_FAM_SBULK, 8, 2, 8, 4, 16384, 8)                                                  \
+    X(95, SWB_FAM_SBULK, 4, 2, 8, 8, 16384, 8)                                                  \
+    X(96, SWB_FAM_SBULK, 4, 3, 8, 4, 16384, 5)                                                  \
+    X(97, SWB_FAM_SBULK, 6, 2, 8, 4, 16384, 8)                                                  \
+    X(98, SWB_FAM_SBULK, 2, 4, 8, 8, 16384, 3)                                                  \
+    X(99, SWB_FAM_SBULK, 8, 3, 8, 4, 16384, 4)
 
 // Ids used when a BULK / RBULK geometry cannot run a shape.
 #define SWB_BULK_FALLBACK_ID 33

@@ -58,8 +58,9 @@ const swb_config_t* find_config(int64_t id) {
     static_assert(FAM != SWB_FAM_LDG || U == 1 || U == 2 || U == 4 || U == 8, "LDG unroll");        \
     static_assert(FAM != SWB_FAM_BULK || (CH % 8 == 0 && CH > 0 && ST >= 2 && (W + 1) * 32 <= 1024), \
                   "BULK geometry");                                                                \
-    static_assert(FAM != SWB_FAM_RBULK || (U >= 1 && U <= 8 && CH >= 16 && ST >= 2 && (W + 1) * 32 <= 1024), \
-                  "RBULK geometry");
+    static_assert((FAM != SWB_FAM_RBULK && FAM != SWB_FAM_SBULK) ||                                \
+                      (U >= 1 && U <= 8 && CH >= 16 && ST >= 2 && (W + 1) * 32 <= 1024),             \
+                  "RBULK/SBULK geometry");
 SWB_CONFIGS(SWB_CHECK)
 #undef SWB_CHECK
 
@@ -227,6 +228,48 @@ struct Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST> {
     template <int MODE>
     static int run(Params p, cudaStream_t s, bool pdl) {
         return launch_rbulk<W, R, U, CH, ST, MODE>(p, s, pdl);
+    }
+};
+
+template <int CW, int CPS, int MAXJ, int STAGE_BYTES, int ST, int MODE>
+int launch_sbulk(Params p, cudaStream_t stream, bool pdl) {
+    constexpr int NM = MODE == MODE_GATE ? 2 : 1;
+    static std::atomic<uint64_t> smem_set{0};
+    const int nv = p.cols / 8;
+    const bool ok = (p.cols % 8) == 0 && (reinterpret_cast<uintptr_t>(p.w) % 16) == 0 &&
+                    (NM == 1 || (reinterpret_cast<uintptr_t>(p.u) % 16) == 0) && nv <= MAXJ * CW * 32;
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const int resident = sms * CPS;
+    const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
+    const size_t row_bytes = size_t(NM) * p.cols * 2;
+    int rs = int(std::max<size_t>(1, STAGE_BYTES / std::max<size_t>(row_bytes, 1)));
+    int stages = 0;
+    for (; rs >= 1; rs = rs > 1 ? rs / 2 : 0) {  // shrink the stage until at least two fit
+        stages = ST;
+        while (stages >= 2 && sbulk_layout(NM, rs, p.cols, stages, CW).total > budget) --stages;
+        if (stages >= 2 || rs == 1) break;
+    }
+    if (!ok || rs < 1 || stages < 2) return dispatch_fallback<MODE>(SWB_RBULK_FALLBACK_ID, p, stream, pdl);
+    // About 16 blocks per resident CTA: the imbalance left at the end is under one block.
+    const int per = (p.rows + resident * 16 - 1) / (resident * 16);
+    const int rpb = std::max(rs, (per + rs - 1) / rs * rs);
+    const int blocks = (p.rows + rpb - 1) / rpb;
+    p.stages = stages;
+    p.row_stage = rs;
+    p.rows_per_block = rpb;
+    const size_t smem = sbulk_layout(NM, rs, p.cols, stages, CW).total;
+    auto kernel = sbulk_kernel<CW, MAXJ, CPS, MODE>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    launch_kernel(kernel, unsigned(blocks), (CW + 1) * 32, smem, stream, pdl, p);
+    return check_launch();
+}
+
+template <int W, int R, int PK, int U, int CH, int ST>
+struct Launcher<SWB_FAM_SBULK, W, R, PK, U, CH, ST> {
+    template <int MODE>
+    static int run(Params p, cudaStream_t s, bool pdl) {
+        return launch_sbulk<W, R, U, CH, ST, MODE>(p, s, pdl);
     }
 };
 

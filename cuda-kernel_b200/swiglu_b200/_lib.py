@@ -42,6 +42,7 @@ SWB_HALF_OUT = 2
 SWB_FAMILY_LDG = 0
 SWB_FAMILY_BULK = 1
 SWB_FAMILY_RBULK = 2
+SWB_FAMILY_SBULK = 3
 SWBL_E_CUBLAS = 100
 
 

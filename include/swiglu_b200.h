@@ -52,6 +52,7 @@ extern "C" {
 #define SWB_FAMILY_LDG 0  /* register-streaming 128/32-bit loads, x staged in shared memory */
 #define SWB_FAMILY_BULK 1 /* persistent: cp.async.bulk ring + mbarriers, one producer warp */
 #define SWB_FAMILY_RBULK 2 /* persistent: whole-row ring stages, x held in registers */
+#define SWB_FAMILY_SBULK 3 /* RBULK with hardware work stealing (cluster launch control) */
 
 /* Host metadata of one launch geometry (include/config.hpp:5 struct Config). */
 typedef struct swb_config {

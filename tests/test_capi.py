@@ -68,7 +68,7 @@ def test_registry_keeps_reference_ids_and_rejects_invalid():
         elif c["family"] == _lib.SWB_FAMILY_BULK:
             assert c["chunk"] % 8 == 0 and c["stages"] >= 2 and (c["warps"] + 1) * 32 <= 1024
         else:
-            assert c["family"] == _lib.SWB_FAMILY_RBULK
+            assert c["family"] in (_lib.SWB_FAMILY_RBULK, _lib.SWB_FAMILY_SBULK)
             assert 1 <= c["unroll"] <= 8 and c["stages"] >= 2 and (c["warps"] + 1) * 32 <= 1024
         if cid in ref_geom:
             assert (c["warps"], c["rows"], c["pack"]) == ref_geom[cid]

@@ -314,3 +314,85 @@ def test_rbulk_covers_the_layer_shapes(configs):
                               (1792, 4096, True), (4096, 1792, False), (7168, 4096, True), (4096, 7168, False)):
         plans = [rbulk_plan(c, rows, cols, gated) for c in configs if c["family"] == 2]
         assert any(p is not None for p in plans), (rows, cols)
+
+
+def sbulk_layout(nm, rs, cols, stages, cw):
+    def up(v, a):
+        return (v + a - 1) // a * a
+    full = up(stages * rs * nm * cols * 2, 16)
+    empty = full + stages * 8
+    meta = empty + stages * 8
+    cnt = meta + stages * 8
+    part = up(cnt + stages * 4, 16)
+    return {"full": full, "empty": empty, "meta": meta, "cnt": cnt, "part": part,
+            "total": up(part + stages * rs * cw * nm * 4, 16)}
+
+
+def sbulk_plan(cfg, rows, cols, gated, w_aligned=True):
+    """Mirror of launch_sbulk: None when the fallback geometry runs."""
+    nm = 2 if gated else 1
+    cw, cps, maxj, target, smax = cfg["warps"], cfg["rows"], cfg["unroll"], cfg["chunk"], cfg["stages"]
+    nv = cols // 8
+    ok = cols % 8 == 0 and w_aligned and nv <= maxj * cw * 32
+    resident = SMS * cps
+    budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 128
+    rs = max(1, target // max(nm * cols * 2, 1))
+    stages = 0
+    while rs >= 1:
+        stages = smax
+        while stages >= 2 and sbulk_layout(nm, rs, cols, stages, cw)["total"] > budget:
+            stages -= 1
+        if stages >= 2 or rs == 1:
+            break
+        rs = rs // 2 if rs > 1 else 0
+    if not ok or rs < 1 or stages < 2:
+        return None
+    per = (rows + resident * 16 - 1) // (resident * 16)
+    rpb = max(rs, (per + rs - 1) // rs * rs)
+    return {"rs": rs, "stages": stages, "rpb": rpb, "blocks": (rows + rpb - 1) // rpb, "budget": budget,
+            "layout": sbulk_layout(nm, rs, cols, stages, cw)}
+
+
+def audit_sbulk(cfg, rows, cols, gated):
+    plan = sbulk_plan(cfg, rows, cols, gated)
+    if plan is None:
+        return False
+    nm = 2 if gated else 1
+    rs, rpb, L = plan["rs"], plan["rpb"], plan["layout"]
+    assert L["total"] <= plan["budget"] and L["full"] % 16 == 0 and L["part"] % 16 == 0
+    assert L["meta"] % 8 == 0 and rpb % rs == 0
+    owner = np.zeros(rows, np.int64)
+    for block in range(plan["blocks"]):  # every CTA index is one block, run by its CTA or its thief
+        b0, b1 = block * rpb, min(block * rpb + rpb, rows)
+        assert b0 < rows
+        for row in range(b0, b1, rs):
+            ru = min(rs, b1 - row)
+            nbytes = ru * cols * 2
+            assert nbytes % 16 == 0 and (2 * row * cols) % 16 == 0 and nbytes * nm < (1 << 20)
+            owner[row:row + ru] += 1
+    assert (owner == 1).all()
+    return True
+
+
+@pytest.mark.parametrize("shape", CORRECTNESS + EXTRA + [(4096, 1792), (4096, 2752), (4096, 1376)])
+def test_sbulk_plan_and_coverage(configs, shape):
+    h, i = shape
+    ran = 0
+    for cfg in configs:
+        if cfg["family"] != 3:
+            continue
+        for rows, cols, gated in ((i, h, True), (h, i, False)):
+            ran += audit_sbulk(cfg, rows, cols, gated)
+    if h % 8 == 0 and i % 8 == 0 and max(h, i) <= 8192:
+        assert ran > 0
+
+
+def test_sbulk_blocks_leave_work_to_steal(configs):
+    """At the layer shapes every resident CTA starts with many blocks left in the grid."""
+    for cfg in configs:
+        if cfg["family"] != 3:
+            continue
+        for rows, cols, gated in ((14336, 4096, True), (4096, 14336, False)):
+            plan = sbulk_plan(cfg, rows, cols, gated)
+            if plan is not None:
+                assert plan["blocks"] >= 4 * SMS * cfg["rows"], (cfg["id"], plan)
