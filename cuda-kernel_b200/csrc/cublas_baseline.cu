@@ -44,6 +44,11 @@ int swbl_create(void** handle) {
     return SWB_OK;
 }
 
+int swbl_version(void* handle, int* out) {
+    if (!handle || !out) return fail(SWB_E_INPUT, "null handle or output");
+    return blas_status(cublasGetVersion(static_cast<cublasHandle_t>(handle), out));
+}
+
 int swbl_destroy(void* handle) {
     if (!handle) return SWB_OK;
     return blas_status(cublasDestroy(static_cast<cublasHandle_t>(handle)));

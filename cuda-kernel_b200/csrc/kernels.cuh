@@ -44,6 +44,8 @@ struct Params {
     int stages;    // bulk_kernel / rbulk_kernel: ring depth
     int row_stage; // rbulk_kernel / sbulk_kernel: whole rows per ring stage
     int rows_per_block;  // sbulk_kernel: rows per CTA index (unit of work stealing)
+    int blocks;          // sbulk_kernel: number of row blocks (= grid size)
+    int block_stride;    // sbulk_kernel: A in row_block = (cta * A) mod blocks, gcd(A, blocks) = 1
 };
 
 template <int MODE>
@@ -714,7 +716,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
         int block = blockIdx.x;
         bool ok = true;
         while (block >= 0 && ok) {
-            const int b0 = block * rpb;
+            // CTA index -> row block through a bijection that spreads consecutive
+            // indices A blocks apart, so the CTAs in flight stream from all over the
+            // matrix rather than one narrow window of it.
+            const int rb = int((long long)block * p.block_stride % p.blocks);
+            const int b0 = rb * rpb;
             const int b1 = min(b0 + rpb, p.rows);
             for (int row = b0; row < b1; row += rs) {
                 if (issued >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) { ok = false; break; }

@@ -11,6 +11,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <numeric>
 #include <string>
 
 #include "kernels.cuh"
@@ -255,9 +256,14 @@ int launch_sbulk(Params p, cudaStream_t stream, bool pdl) {
     const int per = (p.rows + resident * 16 - 1) / (resident * 16);
     const int rpb = std::max(rs, (per + rs - 1) / rs * rs);
     const int blocks = (p.rows + rpb - 1) / rpb;
+    // Smallest stride >= blocks / resident that is coprime with blocks.
+    int stride = std::max(1, blocks / resident);
+    while (std::gcd(stride, blocks) != 1) ++stride;
     p.stages = stages;
     p.row_stage = rs;
     p.rows_per_block = rpb;
+    p.blocks = blocks;
+    p.block_stride = stride;
     const size_t smem = sbulk_layout(NM, rs, p.cols, stages, CW).total;
     auto kernel = sbulk_kernel<CW, MAXJ, CPS, MODE>;
     if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
@@ -339,6 +345,16 @@ const char* swb_status_string(int status) {
 const char* swb_last_error(void) { return g_last_error.c_str(); }
 
 int swb_version(void) { return 1; }
+
+int swb_cuda_versions(int* driver, int* runtime) {
+    int d = 0, r = 0;
+    cudaError_t e = cudaDriverGetVersion(&d);
+    if (e == cudaSuccess) e = cudaRuntimeGetVersion(&r);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    if (driver) *driver = d;
+    if (runtime) *runtime = r;
+    return SWB_OK;
+}
 
 int swb_config_count(void) { return kConfigCount; }
 

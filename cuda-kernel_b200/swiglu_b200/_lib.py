@@ -78,6 +78,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_status_string": ([_i], ctypes.c_char_p),
         "swb_last_error": ([], ctypes.c_char_p),
         "swb_version": ([], _i),
+        "swb_cuda_versions": ([ctypes.POINTER(_i), ctypes.POINTER(_i)], _i),
         "swb_config_count": ([], _i),
         "swb_config_ids": ([ctypes.POINTER(_i), _i], _i),
         "swb_valid_config": ([_i64], _i),
@@ -104,6 +105,7 @@ def _declare_cublas(L: ctypes.CDLL) -> ctypes.CDLL:
         "swbl_create": ([ctypes.POINTER(_vp)], _i),
         "swbl_destroy": ([_vp], _i),
         "swbl_last_error": ([], ctypes.c_char_p),
+        "swbl_version": ([_vp, ctypes.POINTER(_i)], _i),
         "swbl_gemv": ([_vp, _i, _vp, _vp, _vp, _i, _i, _vp], _i),
         "swbl_ffn": ([_vp, _i] + [_vp] * 11 + [_i, _i, _vp], _i),
     }

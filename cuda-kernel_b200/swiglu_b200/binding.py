@@ -160,6 +160,13 @@ def residual_epilogue(y: torch.Tensor, bias: torch.Tensor, x: torch.Tensor, stre
         _lib.check(_lib.lib().swb_residual_epilogue(y.data_ptr(), bias.data_ptr(), x.data_ptr(), y.numel(), s))
 
 
+def cuda_versions() -> tuple[int, int]:
+    """(driver, runtime) versions seen by the native library."""
+    d, r = _lib.ctypes.c_int(), _lib.ctypes.c_int()
+    _lib.check(_lib.lib().swb_cuda_versions(_lib.ctypes.byref(d), _lib.ctypes.byref(r)))
+    return d.value, r.value
+
+
 def device_error(clear: bool = True) -> int:
     """OR of device-side error codes on the current device (synchronises)."""
     out = _lib.ctypes.c_int()
@@ -196,6 +203,11 @@ class CublasBaseline:
             self._check(self._L.swbl_ffn(self.handle, algo, wg.data_ptr(), wu.data_ptr(), wd.data_ptr(),
                                          x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), g.data_ptr(),
                                          u.data_ptr(), h.data_ptr(), y.data_ptr(), hidden, inter, s))
+
+    def version(self) -> int:
+        out = _lib.ctypes.c_int()
+        self._check(self._L.swbl_version(self.handle, _lib.ctypes.byref(out)))
+        return out.value
 
     def close(self) -> None:
         if getattr(self, "handle", None) is not None and self.handle.value:

@@ -70,6 +70,9 @@ SWB_API const char* swb_status_string(int status);
 /* Detail of the last failing call on the calling host thread ("" if none). */
 SWB_API const char* swb_last_error(void);
 SWB_API int swb_version(void);
+/* CUDA driver and runtime versions seen by this library (evidence metadata,
+ * src/benchmark.cu:327-328); the runtime is the one linked into the library. */
+SWB_API int swb_cuda_versions(int* driver, int* runtime);
 
 /* ---- registry: replaces include/config.hpp:7-20 and torch_extension.cu:52 config_ids() ---- */
 SWB_API int swb_config_count(void);

@@ -28,6 +28,8 @@ extern "C" {
 SWB_API int swbl_create(void** handle);
 SWB_API int swbl_destroy(void* handle);
 SWB_API const char* swbl_last_error(void);
+/* cublasGetVersion of the handle (src/benchmark.cu:328). */
+SWB_API int swbl_version(void* handle, int* out);
 
 /* Workload::gemv (src/benchmark.cu:143-150): y[rows] (fp32) = W[rows, cols] x.
  * algo 0 = CUBLAS_GEMM_DEFAULT, 1 = CUBLAS_GEMM_DEFAULT_TENSOR_OP. */

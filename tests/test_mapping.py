@@ -349,7 +349,11 @@ def sbulk_plan(cfg, rows, cols, gated, w_aligned=True):
         return None
     per = (rows + resident * 16 - 1) // (resident * 16)
     rpb = max(rs, (per + rs - 1) // rs * rs)
-    return {"rs": rs, "stages": stages, "rpb": rpb, "blocks": (rows + rpb - 1) // rpb, "budget": budget,
+    blocks = (rows + rpb - 1) // rpb
+    stride = max(1, blocks // resident)
+    while math.gcd(stride, blocks) != 1:
+        stride += 1
+    return {"rs": rs, "stages": stages, "rpb": rpb, "blocks": blocks, "stride": stride, "budget": budget,
             "layout": sbulk_layout(nm, rs, cols, stages, cw)}
 
 
@@ -362,15 +366,18 @@ def audit_sbulk(cfg, rows, cols, gated):
     assert L["total"] <= plan["budget"] and L["full"] % 16 == 0 and L["part"] % 16 == 0
     assert L["meta"] % 8 == 0 and rpb % rs == 0
     owner = np.zeros(rows, np.int64)
+    seen = set()
     for block in range(plan["blocks"]):  # every CTA index is one block, run by its CTA or its thief
-        b0, b1 = block * rpb, min(block * rpb + rpb, rows)
+        rb = block * plan["stride"] % plan["blocks"]
+        seen.add(rb)
+        b0, b1 = rb * rpb, min(rb * rpb + rpb, rows)
         assert b0 < rows
         for row in range(b0, b1, rs):
             ru = min(rs, b1 - row)
             nbytes = ru * cols * 2
             assert nbytes % 16 == 0 and (2 * row * cols) % 16 == 0 and nbytes * nm < (1 << 20)
             owner[row:row + ru] += 1
-    assert (owner == 1).all()
+    assert (owner == 1).all() and len(seen) == plan["blocks"]
     return True
 
 
