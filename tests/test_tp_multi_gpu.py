@@ -1,0 +1,84 @@
+"""Tensor-parallel layer on real GPUs: one process per GPU, NCCL all-reduce.
+
+Each rank runs swb_ffn_tp on its shard (rows of Wg/Wu, columns of Wd), the fp32
+partial y is summed with an NCCL all-reduce, and bias + residual are applied once
+(swb_residual_epilogue). Every rank's y is compared with the unsharded CPU oracle
+at the parity tests' tolerance. Needs at least 2 GPUs; skipped otherwise.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, hidden, inter, q):
+    import datetime
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "cuda-kernel_b200")]
+    import torch
+    import torch.distributed as dist
+    import oracle as O
+    from swiglu_b200 import binding
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        w = O.normal_workload(0, hidden, inter)
+        a, b = rank * inter // world, (rank + 1) * inter // world
+        t = lambda v: torch.from_numpy(np.ascontiguousarray(v)).to(dev)  # noqa: E731
+        wg, wu, wd = t(w["wg"][a:b]), t(w["wu"][a:b]), t(w["wd"][:, a:b])
+        bg, bu, x, bd = t(w["bg"][a:b]), t(w["bu"][a:b]), t(w["x"]), t(w["bd"])
+        h = torch.empty(b - a, dtype=torch.float16, device=dev)
+        y = torch.empty(hidden, dtype=torch.float32, device=dev)
+        out = []
+        for cfg in (33, 69, 87):
+            binding.ffn_tp(x, wg, wu, wd, bg, bu, h, y, cfg, cfg)
+            dist.all_reduce(y)
+            binding.residual_epilogue(y, bd, x)
+            torch.cuda.synchronize()
+            out.append(y.cpu().numpy().copy())
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_nccl_matches_oracle(world):
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    import oracle as O
+    hidden, inter = 4096, 14336
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, hidden, inter, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    w = O.normal_workload(0, hidden, inter)
+    _, act, y_ref = O.ffn(w)
+    atol = 2.0 ** -11 * (np.abs(w["wd"].astype(np.float32)) @ np.abs(act.astype(np.float32)))
+    for rank in range(world):
+        for y in results[rank]:
+            assert np.max(np.abs(y - y_ref) / (np.abs(y_ref) + atol)) <= 2e-3
+            assert O.compare(y, y_ref)[0]
+    for y0, y1 in zip(results[0], results[1]):
+        assert np.array_equal(y0, y1)  # every rank holds the same reduced y
