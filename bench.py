@@ -194,7 +194,8 @@ def ours(args) -> None:
     _lib.lib()  # fail loudly now if the native library is missing
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")  # a timed-out collective ends the process
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=device)
 
     H, I = args.hidden, args.intermediate
     if I % world:
@@ -287,8 +288,12 @@ def ours(args) -> None:
     atol = 2.0 ** -11 * (w0["wd"].float().abs() @ href.float().abs())
     rel = ((y - yref).abs() / (yref.abs() + atol)).max().item()
     del w0, gref, uref, href, yref, atol
+    if world > 1:  # every rank takes the same exit decision
+        t = torch.tensor([rel], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        rel = float(t.item())
     if not rel <= 2e-3:
-        raise SystemExit(f"bench sanity check failed on rank {rank}: max relative error {rel}")
+        raise SystemExit(f"bench sanity check failed: max relative error {rel}")
     launches_per_step = 2 if world == 1 else 3
 
     # ---- one CUDA graph per rotating copy holds the whole step (as the reference
@@ -324,11 +329,16 @@ def ours(args) -> None:
     if world > 1:
         dist.barrier()
     elapsed_ms = start.elapsed_time(end)
+    if world > 1:  # max over ranks; every rank then holds the same number
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
     # A timed region shorter than a few NVML samples is followed by a soak of the same
-    # graph replays (not timed) so the clock record reflects this load.
+    # graph replays (not timed) so the clock record reflects this load. The replay
+    # count comes from the rank-agreed time, so every rank issues the same collectives.
     soak_window = None
-    if t_window[1] - t_window[0] < 0.3:
-        soak_steps = int(math.ceil(0.3 / max(t_window[1] - t_window[0], 1e-4) * args.steps))
+    if elapsed_ms < 300.0:
+        soak_steps = int(math.ceil(300.0 / max(elapsed_ms, 1e-3) * args.steps))
         t0 = time.time()
         for i in range(soak_steps):
             run_step(i)
@@ -336,10 +346,6 @@ def ours(args) -> None:
         soak_window = (t0, time.time())
         if world > 1:
             dist.barrier()
-    if world > 1:
-        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
     us_per_layer = elapsed_ms * 1e3 / args.steps
 
     # ---- dominant kernel (gate): CUDA events around each launch, same rotating copies
