@@ -303,10 +303,9 @@ def ours(args) -> None:
     torch.cuda.synchronize()
     graphs = []
     for c in range(copies):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+        graphs.append(torch.cuda.CUDAGraph())
+        with torch.cuda.graph(graphs[-1], stream=stream):
             step(c)
-        graphs.append(g)
     torch.cuda.synchronize()
 
     def run_step(i):
@@ -373,7 +372,16 @@ def ours(args) -> None:
     # ---- all-reduce alone (tensor parallel): reported separately, it is latency-bound
     tp = None
     if world > 1:
-        ar = time_kernel(torch, lambda i: dist.all_reduce(y), 50, stream)
+        # 20 all-reduces captured in one graph, replayed: device-side latency, not host launch rate
+        ag = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ag, stream=stream):
+            for _ in range(20):
+                dist.all_reduce(y)
+        ag.replay()
+        torch.cuda.synchronize()
+        ar = time_kernel(torch, lambda i: ag.replay(), 10, stream) / 20
+        ag.reset()
+        del ag
         t = torch.tensor([ar], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         tp = {"ranks": world, "shard_rows": shard, "allreduce_us": float(t.item()), "allreduce_bytes": H * 4,
@@ -473,9 +481,13 @@ def ours(args) -> None:
                                  "down": {str(k): round(v, 3) for k, v in tuned["down_times"].items()}}
         print(json.dumps(line), flush=True)
 
-    if graphs is not None:
-        del graphs
+    # Release every graph (some hold NCCL all-reduces) before the process group goes.
+    torch.cuda.synchronize()
+    for gr in graphs:
+        gr.reset()
+    graphs.clear()
     if world > 1:
+        dist.barrier()
         torch.cuda.synchronize()
         dist.destroy_process_group()
 

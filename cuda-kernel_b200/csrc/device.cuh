@@ -162,6 +162,42 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// ------------------------------------------------------ peer-memory signals
+// Upper bound for waiting on another GPU's flag (a peer that died or never
+// launched): the kernel records SWB_DEVERR_PEER_TIMEOUT and skips its output.
+constexpr uint64_t kPeerWaitLimitNs = 1000000000ull;
+
+// Release store at system scope: every store this CTA made before the preceding
+// barrier is visible to whoever acquires this flag, on any GPU.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float ld_volatile_f32(const float* p) {
+    float v;
+    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *f has reached `epoch` (a writer may already be one call ahead).
+__device__ __forceinline__ bool wait_flag_reached(const uint32_t* f, uint32_t epoch) {
+    if (int32_t(ld_acquire_sys(f) - epoch) >= 0) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (int32_t(ld_acquire_sys(f) - epoch) < 0) {
+        if (global_timer_ns() - t0 > kPeerWaitLimitNs) {
+            atomicOr(&g_device_error, 2);
+            return false;
+        }
+    }
+    return true;
+}
+
 // ----------------------------------------------------------- activation
 
 // SiLU(v) = v / (1 + exp(-v)), written in two branches so exp never overflows

@@ -467,28 +467,29 @@ __host__ __device__ inline BulkLayout rbulk_layout(int nm, int row_stage, int co
     return L;
 }
 
-// Persistent row-stage streaming kernel. CTA b owns rows [b*rows/G, (b+1)*rows/G).
+// Persistent row-stage streaming. CTA b owns rows [b*rows/G, (b+1)*rows/G).
 // A producer thread streams them with one cp.async.bulk per matrix per ring
 // stage; a stage holds `row_stage` whole rows, which are contiguous in a
 // row-major matrix. Consumer thread t owns the 16-byte vectors t + j*CT (j <
 // MAXJ) of EVERY row, so its slice of x is loaded once into registers and the
 // only shared-memory traffic is the weights themselves (written by the copy
 // engine, read once by the consumers). Row sums: a warp reduction per row into
-// a fixed slot, combined across warps in a fixed order at the end.
-template <int CW, int MAXJ, int CPS, int MODE>
-__global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params p) {
+// a fixed slot of `part`; `finish(r0, nrows, part)` then runs on the consumer
+// threads (after a consumer barrier) to combine the warps and write the rows.
+// Returns false on the producer warp and when a bounded wait gave up.
+template <int CW, int MAXJ, int MODE>
+__device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* smem, int& r0_out, int& nrows_out,
+                                             float*& part_out) {
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
     constexpr int CT = CW * 32;
-
-    extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_failed;
 
     const int G = gridDim.x;
     const int r0 = int((long long)blockIdx.x * p.rows / G);
     const int r1 = int((long long)(blockIdx.x + 1) * p.rows / G);
     const int nrows = r1 - r0;
-    if (nrows <= 0) return;  // whole CTA leaves together
+    if (nrows <= 0) return false;  // whole CTA leaves together
     const int cols = p.cols;
     const int nv = cols / 8;
     const int rs = p.row_stage;
@@ -502,6 +503,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
     float* part = reinterpret_cast<float*>(smem + L.part);
+    r0_out = r0;
+    nrows_out = nrows;
+    part_out = part;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
 
     if (warp == CW) {
         // ------------------------------------------------------- producer
-        if (lane != 0) return;
+        if (lane != 0) return false;
         const uint64_t pol = l2_evict_first_policy();
         int s = 0, issued = 0;
         uint32_t ph = 0;
@@ -540,7 +544,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
             const int k = issued - j;
             if (!mbar_wait(smem_u32(full + (k % stages)), uint32_t((k / stages) & 1))) break;
         }
-        return;
+        return false;
     }
 
     // ----------------------------------------------------------- consumers
@@ -611,15 +615,95 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
         if (++s == stages) { s = 0; ph ^= 1u; }
     }
     named_barrier_sync(1, CT);
-    if (s_failed) return;
-    for (int i = t; i < nrows; i += CT) {
-        float a = 0.f, b = 0.f;
-        for (int j = 0; j < CW; ++j) {
-            a += part[(size_t(i) * CW + j) * NM];
-            if constexpr (GATED) b += part[(size_t(i) * CW + j) * NM + 1];
-        }
-        write_row<MODE>(p, r0 + i, a, b);
+    return s_failed == 0;
+}
+
+// Sum of warp partials of local row i, in warp order (deterministic).
+template <int CW, int NM>
+__device__ __forceinline__ float row_sum(const float* part, int i, int m) {
+    float a = 0.f;
+    for (int j = 0; j < CW; ++j) a += part[(size_t(i) * CW + j) * NM + m];
+    return a;
+}
+
+template <int CW, int MAXJ, int CPS, int MODE>
+__global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params p) {
+    constexpr int NM = MODE == MODE_GATE ? 2 : 1;
+    constexpr int CT = CW * 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+    int r0, nrows;
+    float* part;
+    if (!rbulk_stream<CW, MAXJ, MODE>(p, smem, r0, nrows, part)) return;
+    for (int i = threadIdx.x; i < nrows; i += CT)
+        write_row<MODE>(p, r0 + i, row_sum<CW, NM>(part, i, 0), NM == 2 ? row_sum<CW, NM>(part, i, NM - 1) : 0.f);
+}
+
+// ============================================ RBULK + one-shot all-reduce
+
+// Tensor-parallel exchange of one layer call. Rank q's exchange buffer holds
+// recv[2][world][rows] fp32 (parity-double-buffered partials from every rank),
+// flags[world][kTpMaxCtas] (flags[src][cta] = call epoch of src's CTA) and this
+// rank's per-CTA call counters.
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpMaxCtas = 1024;
+
+struct TpParams {
+    float* recv[kTpMaxRanks];
+    uint32_t* flags[kTpMaxRanks];
+    uint32_t* ctr;
+    const __half* bias;      // added once after the sum (may be null)
+    const __half* residual;  // added once after the sum (may be null)
+    int rank;
+    int world;
+};
+
+// The down projection of a tensor-parallel rank with the all-reduce fused into
+// its epilogue. Every rank runs the same grid and row partition, so CTA b owns
+// rows [r0, r1) of y on every rank. CTA b: (1) stores its partial rows into
+// slot [parity][my rank] of every rank's receive buffer (NVLink peer stores);
+// (2) publishes flags[my rank][b] = epoch on every rank with a system-scope
+// release; (3) waits (bounded) until every rank's CTA b has published epoch;
+// (4) sums the ranks' partials in rank order -- the same order on every rank, so
+// y is bit-identical everywhere -- adds bias + residual and writes y. The epoch
+// is CTA b's own call counter, so graph replays need no reset; a rank can run at
+// most one call ahead of a peer (it waits on that peer every call), which the
+// parity double buffer and the "reached" flag test cover.
+template <int CW, int MAXJ, int CPS>
+__global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(const Params p, const TpParams tp) {
+    constexpr int CT = CW * 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint32_t s_epoch;
+    __shared__ int s_ok;
+    int r0, nrows;
+    float* part;
+    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part)) return;
+    const int t = threadIdx.x, b = blockIdx.x, rows = p.rows;
+    if (t == 0) {
+        s_epoch = tp.ctr[b] + 1u;
+        s_ok = 1;
     }
+    named_barrier_sync(1, CT);
+    const uint32_t epoch = s_epoch;
+    const size_t par = epoch & 1u;
+    for (int i = t; i < nrows; i += CT) {
+        const float a = row_sum<CW, 1>(part, i, 0);
+        for (int q = 0; q < tp.world; ++q) tp.recv[q][(par * tp.world + tp.rank) * rows + r0 + i] = a;
+    }
+    named_barrier_sync(1, CT);
+    if (t < tp.world) st_release_sys(tp.flags[t] + size_t(tp.rank) * kTpMaxCtas + b, epoch);
+    if (t < tp.world && !wait_flag_reached(tp.flags[tp.rank] + size_t(t) * kTpMaxCtas + b, epoch)) s_ok = 0;
+    named_barrier_sync(1, CT);
+    if (!s_ok) return;
+    const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
+    for (int i = t; i < nrows; i += CT) {
+        float acc = 0.f;
+        for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + r0 + i);
+        float add = 0.f;
+        if (tp.bias) add += __half2float(tp.bias[r0 + i]);
+        if (tp.residual) add += __half2float(tp.residual[r0 + i]);
+        p.y[r0 + i] = acc + add;
+    }
+    if (t == 0) tp.ctr[b] = epoch;
 }
 
 // ===================================================================== SBULK

@@ -11,6 +11,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <new>
 #include <numeric>
 #include <string>
 
@@ -224,11 +225,63 @@ int launch_rbulk(Params p, cudaStream_t stream, bool pdl) {
     return check_launch();
 }
 
+// The fused tensor-parallel down projection (rbulk_allreduce_kernel). Every rank
+// must launch the same grid: the plan depends only on the shape, the geometry
+// and the SM count, which match across ranks of one machine.
+template <int CW, int CPS, int MAXJ, int STAGE_BYTES, int ST>
+int launch_rbulk_ar(Params p, const TpParams& tp, cudaStream_t stream, bool pdl) {
+    static std::atomic<uint64_t> smem_set{0};
+    const int nv = p.cols / 8;
+    if ((p.cols % 8) != 0 || (reinterpret_cast<uintptr_t>(p.w) % 16) != 0 || nv > MAXJ * CW * 32)
+        return fail(SWB_E_UNSUPPORTED, "fused tensor-parallel path needs cols % 8 == 0, 16-byte rows and "
+                                       "cols <= 8 * 32 * warps * unroll of the geometry");
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const int G = std::min(sms * CPS, p.rows);
+    if (G > kTpMaxCtas) return fail(SWB_E_UNSUPPORTED, "grid larger than the exchange flag table");
+    const int rows_per_cta = (p.rows + G - 1) / G;
+    const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
+    const size_t row_bytes = size_t(p.cols) * 2;
+    int rs = int(std::max<size_t>(1, STAGE_BYTES / std::max<size_t>(row_bytes, 1)));
+    rs = std::min(rs, rows_per_cta);
+    int stages = 0;
+    for (; rs >= 1; rs = rs > 1 ? rs / 2 : 0) {
+        stages = ST;
+        while (stages >= 2 && rbulk_layout(1, rs, p.cols, stages, CW, rows_per_cta).total > budget) --stages;
+        if (stages >= 2 || rs == 1) break;
+    }
+    if (rs < 1 || stages < 2) return fail(SWB_E_UNSUPPORTED, "shape does not fit the geometry's shared memory");
+    p.stages = stages;
+    p.row_stage = rs;
+    const size_t smem = rbulk_layout(1, rs, p.cols, stages, CW, rows_per_cta).total;
+    auto kernel = rbulk_allreduce_kernel<CW, MAXJ, CPS>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    if (!pdl) {
+        kernel<<<unsigned(G), (CW + 1) * 32, smem, stream>>>(p, tp);
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(G));
+        cfg.blockDim = dim3((CW + 1) * 32);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, kernel, p, tp);
+    }
+    return check_launch();
+}
+
 template <int W, int R, int PK, int U, int CH, int ST>
 struct Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST> {
     template <int MODE>
     static int run(Params p, cudaStream_t s, bool pdl) {
         return launch_rbulk<W, R, U, CH, ST, MODE>(p, s, pdl);
+    }
+    static int run_allreduce(const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
+        return launch_rbulk_ar<W, R, U, CH, ST>(p, tp, s, pdl);
     }
 };
 
@@ -278,6 +331,34 @@ struct Launcher<SWB_FAM_SBULK, W, R, PK, U, CH, ST> {
         return launch_sbulk<W, R, U, CH, ST, MODE>(p, s, pdl);
     }
 };
+
+template <int FAM>
+struct AllreduceDispatch {
+    template <int W, int R, int PK, int U, int CH, int ST>
+    static int run(const Params&, const TpParams&, cudaStream_t, bool) {
+        return fail(SWB_E_CONFIG_INVALID, "the fused tensor-parallel path needs an RBULK geometry");
+    }
+};
+
+template <>
+struct AllreduceDispatch<SWB_FAM_RBULK> {
+    template <int W, int R, int PK, int U, int CH, int ST>
+    static int run(const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
+        return Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST>::run_allreduce(p, tp, s, pdl);
+    }
+};
+
+int dispatch_allreduce(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
+    switch (id) {
+#define SWB_AR_CASE(ID, FAM, W, R, PK, U, CH, ST) \
+    case ID:                                      \
+        return AllreduceDispatch<FAM>::template run<W, R, PK, U, CH, ST>(p, tp, s, pdl);
+        SWB_CONFIGS(SWB_AR_CASE)
+#undef SWB_AR_CASE
+        default:
+            return fail(SWB_E_CONFIG);
+    }
+}
 
 template <int MODE>
 int dispatch(int64_t id, const Params& p, cudaStream_t s, bool pdl = false) {
@@ -537,3 +618,115 @@ extern "C" int swb_ffn_noalloc(int gate_config, int down_config, const void* wg,
     if (int rc = noalloc_workspace(&h)) return rc;
     return swb_ffn(gate_config, down_config, wg, wu, wd, x, bg, bu, bd, h, y, hidden, inter, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchange: one per rank, allocated once at set-up.
+struct swb_tp {
+    int rank, world, rows, device;
+    void* local;
+    size_t bytes, recv_bytes, flag_bytes;
+    void* peer[kTpMaxRanks];
+    bool connected;
+};
+
+namespace {
+size_t tp_recv_bytes(int world, int rows) { return align_up(size_t(2) * world * rows * 4, 256); }
+size_t tp_flag_bytes(int world) { return align_up(size_t(world) * kTpMaxCtas * 4, 256); }
+}  // namespace
+
+extern "C" {
+
+int swb_tp_create(int rank, int world, int rows, swb_tp_t** out) {
+    if (!out || world < 1 || world > kTpMaxRanks || rank < 0 || rank >= world || rows <= 0)
+        return fail(SWB_E_INPUT, "rank, world (1..8) or rows out of range");
+    swb_tp* tp = new (std::nothrow) swb_tp();
+    if (!tp) return fail(SWB_E_INPUT, "out of host memory");
+    tp->rank = rank;
+    tp->world = world;
+    tp->rows = rows;
+    tp->recv_bytes = tp_recv_bytes(world, rows);
+    tp->flag_bytes = tp_flag_bytes(world);
+    tp->bytes = tp->recv_bytes + tp->flag_bytes + align_up(size_t(kTpMaxCtas) * 4, 256);
+    cudaError_t e = cudaGetDevice(&tp->device);
+    if (e == cudaSuccess) e = cudaMalloc(&tp->local, tp->bytes);  // set-up time, once per rank
+    if (e == cudaSuccess) e = cudaMemset(tp->local, 0, tp->bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        if (tp->local) cudaFree(tp->local);
+        delete tp;
+        return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    }
+    for (int q = 0; q < kTpMaxRanks; ++q) tp->peer[q] = nullptr;
+    tp->peer[rank] = tp->local;
+    tp->connected = world == 1;
+    *out = tp;
+    return SWB_OK;
+}
+
+int swb_tp_ipc_handle(const swb_tp_t* tp, void* out) {
+    if (!tp || !out) return fail(SWB_E_INPUT, "null exchange or output");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, tp->local);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    static_assert(sizeof(h) == SWB_TP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(out, &h, sizeof h);
+    return SWB_OK;
+}
+
+int swb_tp_connect(swb_tp_t* tp, const void* handles) {
+    if (!tp || !handles) return fail(SWB_E_INPUT, "null exchange or handles");
+    if (tp->connected) return SWB_OK;
+    for (int q = 0; q < tp->world; ++q) {
+        if (q == tp->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const char*>(handles) + size_t(q) * SWB_TP_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+        tp->peer[q] = p;
+    }
+    tp->connected = true;
+    return SWB_OK;
+}
+
+int swb_tp_destroy(swb_tp_t* tp) {
+    if (!tp) return SWB_OK;
+    for (int q = 0; q < tp->world; ++q)
+        if (q != tp->rank && tp->peer[q]) cudaIpcCloseMemHandle(tp->peer[q]);
+    if (tp->local) cudaFree(tp->local);
+    delete tp;
+    return SWB_OK;
+}
+
+int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
+                     const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard, const void* bd,
+                     void* h_shard, float* y, int hidden, int shard, void* stream) {
+    if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
+    if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
+    if (!wd_shard || !x) return fail(SWB_E_INPUT);
+    if (!y) return fail(SWB_E_FLOAT_OUTPUT);
+    if (int rc = swb_gate(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream))
+        return rc;
+    Params p = make_params();
+    p.w = static_cast<const __half*>(wd_shard);
+    p.x = static_cast<const __half*>(h_shard);
+    p.y = y;
+    p.rows = hidden;
+    p.cols = shard;
+    TpParams t;
+    std::memset(&t, 0, sizeof t);
+    for (int q = 0; q < tp->world; ++q) {
+        char* base = static_cast<char*>(tp->peer[q]);
+        t.recv[q] = reinterpret_cast<float*>(base);
+        t.flags[q] = reinterpret_cast<uint32_t*>(base + tp->recv_bytes);
+    }
+    t.ctr = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + tp->flag_bytes);
+    t.bias = static_cast<const __half*>(bd);
+    t.residual = static_cast<const __half*>(x);
+    t.rank = tp->rank;
+    t.world = tp->world;
+    return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true);
+}
+
+}  // extern "C"

@@ -37,6 +37,9 @@ SWB_E_DEVICE = 13
 SWB_E_UNSUPPORTED = 14
 SWB_E_WORKSPACE = 15
 SWB_NOALLOC_MAX_INTER = 65536
+SWB_TP_MAX_RANKS = 8
+SWB_TP_HANDLE_BYTES = 64
+SWB_DEVERR_PEER_TIMEOUT = 2
 SWB_RESIDUAL = 1
 SWB_HALF_OUT = 2
 SWB_FAMILY_LDG = 0
@@ -89,6 +92,11 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_ffn_tp": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_ffn_noalloc": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_swiglu_out": ([_vp] * 6 + [_i64] * 4 + [_vp], _i),
+        "swb_tp_create": ([_i, _i, _i, ctypes.POINTER(_vp)], _i),
+        "swb_tp_ipc_handle": ([_vp, _vp], _i),
+        "swb_tp_connect": ([_vp, _vp], _i),
+        "swb_tp_destroy": ([_vp], _i),
+        "swb_ffn_tp_fused": ([_vp, _i, _i] + [_vp] * 10 + [_i, _i, _vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),
         "swb_residual_epilogue": ([_vp, _vp, _vp, _i, _vp], _i),
         "swb_device_error": ([_i, ctypes.POINTER(_i)], _i),

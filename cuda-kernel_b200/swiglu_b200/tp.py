@@ -1,0 +1,82 @@
+"""Tensor-parallel layer: one process per GPU, fused all-reduce over peer memory.
+
+Rank r of n holds rows [r*I/n, (r+1)*I/n) of Wg and Wu and the same columns of Wd
+(stored contiguously). ``Exchange`` sets up the rank's exchange buffer once:
+it allocates it (C ABI ``swb_tp_create``), shares its CUDA IPC handle with every
+rank through ``torch.distributed`` and maps the peers' buffers
+(``swb_tp_connect``). ``ffn_tp_fused`` then runs a rank's layer as two kernels:
+the gate on the shard, and the down projection whose epilogue stores its partial
+rows into every rank's buffer over NVLink, waits for the peers' flags and writes
+y = sum of partials + bias + residual (identical on every rank). ``shard`` cuts
+the weights for a rank. The NCCL alternative (``swb_ffn_tp`` + all-reduce +
+``swb_residual_epilogue``) stays available as the baseline.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def shard(wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, bg, bu, rank: int, world: int) -> dict:
+    """Rank `rank`'s contiguous shards of the layer's weights (and gate biases)."""
+    inter = wg.shape[0]
+    if inter % world:
+        raise ValueError("intermediate size must divide by the rank count")
+    a, b = rank * inter // world, (rank + 1) * inter // world
+    out = {"wg": wg[a:b].contiguous(), "wu": wu[a:b].contiguous(), "wd": wd[:, a:b].contiguous()}
+    out["bg"] = None if bg is None else bg[a:b].contiguous()
+    out["bu"] = None if bu is None else bu[a:b].contiguous()
+    return out
+
+
+class Exchange:
+    """This rank's fused-all-reduce exchange buffer, mapped into every rank."""
+
+    def __init__(self, rank: int, world: int, rows: int, device: torch.device, group=None):
+        import torch.distributed as dist
+        self.rank, self.world, self.rows, self.device = rank, world, rows, device
+        L = _lib.lib()
+        self._ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(L.swb_tp_create(rank, world, rows, ctypes.byref(self._ptr)))
+            mine = (ctypes.c_uint8 * _lib.SWB_TP_HANDLE_BYTES)()
+            _lib.check(L.swb_tp_ipc_handle(self._ptr, mine))
+            if world > 1:
+                gathered = [None] * world
+                dist.all_gather_object(gathered, bytes(mine), group=group)
+            else:
+                gathered = [bytes(mine)]
+            table = (ctypes.c_uint8 * (_lib.SWB_TP_HANDLE_BYTES * world)).from_buffer_copy(b"".join(gathered))
+            _lib.check(L.swb_tp_connect(self._ptr, table))
+
+    @property
+    def handle(self):
+        return self._ptr
+
+    def close(self) -> None:
+        if self._ptr is not None and self._ptr.value:
+            with torch.cuda.device(self.device):
+                _lib.lib().swb_tp_destroy(self._ptr)
+            self._ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ffn_tp_fused(ex: Exchange, x: torch.Tensor, s: dict, bd: torch.Tensor | None, h: torch.Tensor,
+                 y: torch.Tensor, gate_config: int, down_config: int, stream: int | None = None) -> None:
+    """One rank's layer with the fused all-reduce; y (fp32 [hidden]) ends identical on every rank."""
+    shard_rows, hidden = s["wg"].shape
+    sp = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().swb_ffn_tp_fused(ex.handle, int(gate_config), int(down_config), s["wg"].data_ptr(),
+                                               s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), ptr(s["bg"]),
+                                               ptr(s["bu"]), ptr(bd), h.data_ptr(), y.data_ptr(), hidden,
+                                               shard_rows, sp))

@@ -135,6 +135,32 @@ SWB_API int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, c
                        const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard,
                        void* h_shard, float* y_partial, int hidden, int shard, void* stream);
 
+/* Fused tensor parallel (no counterpart in the reference). The down projection of
+ * each rank sums the ranks' partial y itself: its CTAs store their partial rows
+ * straight into every peer's exchange buffer over NVLink, publish a flag with a
+ * system-scope release, wait (bounded: SWB_DEVERR_PEER_TIMEOUT, then no output)
+ * for the same CTA of every rank, and add the partials in rank order plus bias
+ * and residual -- no NCCL call and no separate epilogue kernel. Set-up, once per
+ * rank: swb_tp_create (allocates this rank's exchange buffer), share
+ * swb_tp_ipc_handle with every rank (any transport), swb_tp_connect with all
+ * handles in rank order. Every rank must then make the same sequence of
+ * swb_ffn_tp_fused calls with the same shapes and geometries (one exchange per
+ * stream of calls; calls on one exchange must not overlap). */
+#define SWB_DEVERR_PEER_TIMEOUT 2
+#define SWB_TP_MAX_RANKS 8
+#define SWB_TP_HANDLE_BYTES 64
+typedef struct swb_tp swb_tp_t;
+SWB_API int swb_tp_create(int rank, int world, int rows, swb_tp_t** out);
+SWB_API int swb_tp_ipc_handle(const swb_tp_t* tp, void* out);
+SWB_API int swb_tp_connect(swb_tp_t* tp, const void* handles);
+SWB_API int swb_tp_destroy(swb_tp_t* tp);
+/* One rank's whole layer: gate on its shard, then the fused down + all-reduce;
+ * y: [hidden] fp32, identical on every rank. down_config must be an RBULK id. */
+SWB_API int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard,
+                             const void* wu_shard, const void* wd_shard, const void* x, const void* bg_shard,
+                             const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,
+                             void* stream);
+
 /* swiglu_out, src/torch_extension.cu:7-40: the binding's shape / config / alias guards,
  * then the model-rounding gate into h [inter] and the fp16 down projection into
  * y [hidden] (no bias, no residual -- the residual stays in the transformer layer).

@@ -151,3 +151,14 @@ def test_decode_swiglu_dropin_module():
     from swiglu_b200 import binding
     assert ext.swiglu_out is binding.swiglu_out and ext.swiglu is binding.swiglu
     assert ext.config_ids() == binding.config_ids()
+
+
+def test_tp_exchange_guards_without_gpu():
+    out = ctypes.c_void_p()
+    for rank, world, rows in ((0, 0, 16), (0, 9, 16), (2, 2, 16), (-1, 2, 16), (0, 2, 0)):
+        assert L().swb_tp_create(rank, world, rows, ctypes.byref(out)) == _lib.SWB_E_INPUT
+    assert L().swb_tp_ipc_handle(None, None) == _lib.SWB_E_INPUT
+    assert L().swb_tp_connect(None, None) == _lib.SWB_E_INPUT
+    assert L().swb_tp_destroy(None) == _lib.SWB_OK
+    f = L().swb_ffn_tp_fused
+    assert f(None, 83, 83, *([FAKE] * 10), 64, 32, None) == _lib.SWB_E_INPUT

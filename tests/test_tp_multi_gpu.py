@@ -50,6 +50,18 @@ def _rank(rank, world, port, hidden, inter, q):
             binding.residual_epilogue(y, bd, x)
             torch.cuda.synchronize()
             out.append(y.cpu().numpy().copy())
+        # the fused path: down projection + all-reduce over peer memory + epilogue in one kernel
+        from swiglu_b200 import tp as T
+        ex = T.Exchange(rank, world, hidden, dev)
+        s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
+        for down in (80, 83, 87, 87, 87):
+            y.zero_()
+            T.ffn_tp_fused(ex, x, s, bd, h, y, 69, down)
+            torch.cuda.synchronize()
+            out.append(y.cpu().numpy().copy())
+        dist.barrier()
+        assert binding.device_error() == 0
+        ex.close()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
