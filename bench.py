@@ -8,8 +8,10 @@ twice the 126 MB L2, so every step streams its weights from HBM.
 
 * N = 1: the two product kernels (gate, down) on one B200.
 * N > 1 (torchrun, one rank per GPU): tensor parallel. Wg/Wu split by
-  intermediate row, Wd by its K dimension; one NCCL all-reduce of the fp32 y,
-  then bias + residual once. Each rank's step is captured in a CUDA graph.
+  intermediate row, Wd by its K dimension; the down kernel sums the ranks'
+  partial y over NVLink peer memory and adds bias + residual once (fused
+  all-reduce). The NCCL all-reduce path is timed beside it as the baseline.
+  Each rank's step is captured in a CUDA graph.
 
 Prints ONE JSON line on rank 0. ``--impl reference`` times the reference's own
 CPU path (its include/contract.hpp matvec, compiled under oracle/_ref) on the
@@ -128,12 +130,12 @@ def time_kernel(torch, fn, reps, stream):
     return start.elapsed_time(end) * 1e3 / reps
 
 
-def tune(torch, binding, launch_gate, launch_down, ids, stream, reps=8):
+def tune(torch, binding, launch_gate, launch_down, ids, stream, reps=8, down_ids=None):
     """Pick the fastest gate and down geometry by median over rotating copies."""
     best = {}
-    for name, launch in (("gate", launch_gate), ("down", launch_down)):
+    for name, launch, cand in (("gate", launch_gate, ids), ("down", launch_down, down_ids or ids)):
         times = {}
-        for cid in ids:
+        for cid in cand:
             launch(cid, 0)
             torch.cuda.synchronize()
             samples = [time_kernel(torch, lambda i, c=cid: launch(c, i), reps, stream) for _ in range(3)]
@@ -251,10 +253,14 @@ def ours(args) -> None:
                                      0, sp))
 
     ids = binding.config_ids()
+    down_ids = ids
+    if world > 1:
+        # the fused all-reduce epilogue lives in the RBULK kernel: tune the down geometry among those
+        down_ids = [c for c in ids if binding.config_info(c)["family"] == _lib.SWB_FAMILY_RBULK]
     if args.gate_config and args.down_config:
         gcfg, dcfg, tuned = args.gate_config, args.down_config, None
     else:
-        tuned = tune(torch, binding, launch_gate, launch_down, ids, stream)
+        tuned = tune(torch, binding, launch_gate, launch_down, ids, stream, down_ids=down_ids)
         gcfg = args.gate_config or tuned["gate"]
         dcfg = args.down_config or tuned["down"]
         if world > 1:  # every rank runs the same geometry: take rank 0's choice
@@ -262,19 +268,32 @@ def ours(args) -> None:
             dist.broadcast(t, 0)
             gcfg, dcfg = int(t[0]), int(t[1])
 
+    exchange = None
+    if world > 1:
+        from swiglu_b200.tp import Exchange
+        exchange = Exchange(rank, world, H, device)  # one-time set-up: IPC handles shared by all_gather
+
     def step(i):
-        # the layer entry points: gate kernel, then the down kernel launched programmatically
+        # the layer entry points: gate kernel, then the down kernel launched programmatically;
+        # for N > 1 the down kernel also sums the ranks' partials over NVLink (fused all-reduce)
         s = sets[i % copies]
         if world == 1:
             _lib.check(L.swb_ffn(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
                                  x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
                                  y.data_ptr(), H, shard, sp))
         else:
-            _lib.check(L.swb_ffn_tp(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
-                                    x.data_ptr(), bg.data_ptr(), bu.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard,
-                                    sp))
-            dist.all_reduce(y)
-            _lib.check(L.swb_residual_epilogue(y.data_ptr(), bd.data_ptr(), x.data_ptr(), H, sp))
+            _lib.check(L.swb_ffn_tp_fused(exchange.handle, gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(),
+                                          s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(), bu.data_ptr(),
+                                          bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard, sp))
+
+    def step_nccl(i):
+        # the baseline tensor-parallel step: partial y, NCCL all-reduce, then bias + residual
+        s = sets[i % copies]
+        _lib.check(L.swb_ffn_tp(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                x.data_ptr(), bg.data_ptr(), bu.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard,
+                                sp))
+        dist.all_reduce(y)
+        _lib.check(L.swb_residual_epilogue(y.data_ptr(), bd.data_ptr(), x.data_ptr(), H, sp))
 
     # ---- sanity check of the (sharded) layer against a plain torch fp32 computation
     step(0)
@@ -294,7 +313,15 @@ def ours(args) -> None:
         rel = float(t.item())
     if not rel <= 2e-3:
         raise SystemExit(f"bench sanity check failed: max relative error {rel}")
-    launches_per_step = 2 if world == 1 else 3
+    if world > 1:  # the NCCL baseline must agree with the fused path too
+        y_fused = y.clone()
+        step_nccl(0)
+        torch.cuda.synchronize()
+        dn = ((y - y_fused).abs() / (y_fused.abs() + 1e-6)).max()
+        dist.all_reduce(dn, op=dist.ReduceOp.MAX)
+        if not float(dn) <= 1e-5:
+            raise SystemExit(f"fused and NCCL tensor-parallel paths disagree: {float(dn)}")
+    launches_per_step = 2
 
     # ---- one CUDA graph per rotating copy holds the whole step (as the reference
     # times its candidates: src/benchmark.cu:46-83); for N > 1 it includes the NCCL all-reduce
@@ -372,6 +399,25 @@ def ours(args) -> None:
     # ---- all-reduce alone (tensor parallel): reported separately, it is latency-bound
     tp = None
     if world > 1:
+        # the NCCL baseline step, captured and timed the same way (max over ranks)
+        ngraphs = []
+        for c in range(copies):
+            step_nccl(c)
+        torch.cuda.synchronize()
+        for c in range(copies):
+            ngraphs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(ngraphs[-1], stream=stream):
+                step_nccl(c)
+        for i in range(args.warmup):
+            ngraphs[i % copies].replay()
+        dist.barrier()
+        nccl_us = time_kernel(torch, lambda i: ngraphs[i % copies].replay(), args.steps, stream)
+        for gr in ngraphs:
+            gr.reset()
+        ngraphs.clear()
+        t = torch.tensor([nccl_us], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl_us = float(t.item())
         # 20 all-reduces captured in one graph, replayed: device-side latency, not host launch rate
         ag = torch.cuda.CUDAGraph()
         with torch.cuda.graph(ag, stream=stream):
@@ -384,13 +430,35 @@ def ours(args) -> None:
         del ag
         t = torch.tensor([ar], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        tp = {"ranks": world, "shard_rows": shard, "allreduce_us": float(t.item()), "allreduce_bytes": H * 4,
-              "backend": "nccl"}
+        tp = {"ranks": world, "shard_rows": shard, "exchange": "fused one-shot all-reduce over NVLink peer memory "
+              "in the down kernel", "nccl_step_us": nccl_us, "fused_speedup_vs_nccl": nccl_us / us_per_layer,
+              "nccl_allreduce_us": float(t.item()), "allreduce_bytes": H * 4}
 
     # ---- end to end through the public C-ABI call with host buffers (N=1). As the
     # reference's transfer-inclusive timing (src/benchmark.cu:177-206): each step copies
     # x from pinned host memory, runs the captured layer call, copies y back to pinned host.
     e2e = None
+    if world > 1:
+        # every rank: pinned H2D of x, the captured layer step, D2H of y (max over ranks)
+        x_host = x.cpu().pin_memory()
+        y_host = torch.empty(H, dtype=torch.float32).pin_memory()
+        x_keep = x.clone()
+
+        def e2e_step_tp(i):
+            x.copy_(x_host, non_blocking=True)
+            graphs[i % copies].replay()
+            y_host.copy_(y, non_blocking=True)
+
+        for i in range(max(args.warmup, 3)):
+            e2e_step_tp(i)
+        dist.barrier()
+        e2e_us = time_kernel(torch, e2e_step_tp, args.steps, stream)
+        t = torch.tensor([e2e_us], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        x.copy_(x_keep)
+        e2e = {"value": float(t.item()), "unit": UNIT, "h2d_bytes_per_step": world * H * 2,
+               "d2h_bytes_per_step": world * H * 4,
+               "path": "every rank: pinned host x -> H2D -> captured swb_ffn_tp_fused (C ABI) -> D2H -> pinned host y"}
     if world == 1:
         x_host = common["x"].cpu().pin_memory()
         y_host = torch.empty(H, dtype=torch.float32).pin_memory()
@@ -489,6 +557,8 @@ def ours(args) -> None:
     if world > 1:
         dist.barrier()
         torch.cuda.synchronize()
+        exchange.close()  # every rank is past its last fused call (barrier above)
+        dist.barrier()
         dist.destroy_process_group()
 
 
