@@ -96,7 +96,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_tp_ipc_handle": ([_vp, _vp], _i),
         "swb_tp_connect": ([_vp, _vp], _i),
         "swb_tp_destroy": ([_vp], _i),
-        "swb_ffn_tp_fused": ([_vp, _i, _i] + [_vp] * 10 + [_i, _i, _vp], _i),
+        "swb_ffn_tp_fused": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, _vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),
         "swb_residual_epilogue": ([_vp, _vp, _vp, _i, _vp], _i),
         "swb_device_error": ([_i, ctypes.POINTER(_i)], _i),
@@ -162,6 +162,18 @@ def check(status: int) -> None:
     if status:
         msg = last_error() or status_message(status)
         raise RuntimeError(msg)
+
+
+def declared_signatures() -> dict[str, int]:
+    """Number of parameters of every function the public headers declare."""
+    import re
+    out = {}
+    for h in HEADERS:
+        text = h.read_text()
+        for m in re.finditer(r"^SWB_API\s+(?:const\s+)?\w+\*?\s+(\w+)\(([^;]*?)\);", text, flags=re.M | re.S):
+            params = " ".join(m.group(2).split())
+            out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
 
 
 def declared_symbols() -> list[str]:

@@ -161,4 +161,14 @@ def test_tp_exchange_guards_without_gpu():
     assert L().swb_tp_connect(None, None) == _lib.SWB_E_INPUT
     assert L().swb_tp_destroy(None) == _lib.SWB_OK
     f = L().swb_ffn_tp_fused
-    assert f(None, 83, 83, *([FAKE] * 10), 64, 32, None) == _lib.SWB_E_INPUT
+    assert f(None, 83, 83, *([FAKE] * 9), 64, 32, None) == _lib.SWB_E_INPUT
+
+
+def test_ctypes_declarations_match_header_arity():
+    """Every typed entry point takes exactly as many arguments as the header declares."""
+    sigs = _lib.declared_signatures()
+    assert len(sigs) == len(_lib.declared_symbols())
+    for name, nparams in sigs.items():
+        fn = getattr(_lib.cublas_lib() if name.startswith("swbl_") else L(), name)
+        assert fn.argtypes is not None, name
+        assert len(fn.argtypes) == nparams, (name, len(fn.argtypes), nparams)

@@ -36,35 +36,43 @@ def _rank(rank, world, port, hidden, inter, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     try:
-        w = O.normal_workload(0, hidden, inter)
-        a, b = rank * inter // world, (rank + 1) * inter // world
-        t = lambda v: torch.from_numpy(np.ascontiguousarray(v)).to(dev)  # noqa: E731
-        wg, wu, wd = t(w["wg"][a:b]), t(w["wu"][a:b]), t(w["wd"][:, a:b])
-        bg, bu, x, bd = t(w["bg"][a:b]), t(w["bu"][a:b]), t(w["x"]), t(w["bd"])
-        h = torch.empty(b - a, dtype=torch.float16, device=dev)
-        y = torch.empty(hidden, dtype=torch.float32, device=dev)
-        out = []
-        for cfg in (33, 69, 87):
-            binding.ffn_tp(x, wg, wu, wd, bg, bu, h, y, cfg, cfg)
-            dist.all_reduce(y)
-            binding.residual_epilogue(y, bd, x)
-            torch.cuda.synchronize()
-            out.append(y.cpu().numpy().copy())
-        # the fused path: down projection + all-reduce over peer memory + epilogue in one kernel
-        from swiglu_b200 import tp as T
-        ex = T.Exchange(rank, world, hidden, dev)
-        s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
-        for down in (80, 83, 87, 87, 87):
-            y.zero_()
-            T.ffn_tp_fused(ex, x, s, bd, h, y, 69, down)
-            torch.cuda.synchronize()
-            out.append(y.cpu().numpy().copy())
-        dist.barrier()
-        assert binding.device_error() == 0
-        ex.close()
-        q.put((rank, out))
+        _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding)
+    except BaseException as exc:  # report to the parent at once instead of letting it wait
+        import traceback
+        q.put((rank, "error: " + "".join(traceback.format_exception(exc))))
+        raise
     finally:
         dist.destroy_process_group()
+
+
+def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
+    w = O.normal_workload(0, hidden, inter)
+    a, b = rank * inter // world, (rank + 1) * inter // world
+    t = lambda v: torch.from_numpy(np.ascontiguousarray(v)).to(dev)  # noqa: E731
+    wg, wu, wd = t(w["wg"][a:b]), t(w["wu"][a:b]), t(w["wd"][:, a:b])
+    bg, bu, x, bd = t(w["bg"][a:b]), t(w["bu"][a:b]), t(w["x"]), t(w["bd"])
+    h = torch.empty(b - a, dtype=torch.float16, device=dev)
+    y = torch.empty(hidden, dtype=torch.float32, device=dev)
+    out = []
+    for cfg in (33, 69, 87):
+        binding.ffn_tp(x, wg, wu, wd, bg, bu, h, y, cfg, cfg)
+        dist.all_reduce(y)
+        binding.residual_epilogue(y, bd, x)
+        torch.cuda.synchronize()
+        out.append(y.cpu().numpy().copy())
+    # the fused path: down projection + all-reduce over peer memory + epilogue in one kernel
+    from swiglu_b200 import tp as T
+    ex = T.Exchange(rank, world, hidden, dev)
+    s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
+    for down in (80, 83, 87, 87, 87):
+        y.zero_()
+        T.ffn_tp_fused(ex, x, s, bd, h, y, 69, down)
+        torch.cuda.synchronize()
+        out.append(y.cpu().numpy().copy())
+    dist.barrier()
+    assert binding.device_error() == 0
+    ex.close()
+    q.put((rank, out))
 
 
 @pytest.mark.parametrize("world", [2])
@@ -81,7 +89,11 @@ def test_tp_nccl_matches_oracle(world):
     procs = [ctx.Process(target=_rank, args=(r, world, port, hidden, inter, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=300) for _ in range(world))
+    results = {}
+    for _ in range(world):
+        rank, out = q.get(timeout=300)
+        assert not isinstance(out, str), out
+        results[rank] = out
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
