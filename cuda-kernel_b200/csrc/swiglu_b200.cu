@@ -348,7 +348,24 @@ struct AllreduceDispatch<SWB_FAM_RBULK> {
     }
 };
 
+int dispatch_allreduce_one(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl);
+
+// RBULK geometries tried, in order, when the requested one cannot hold a row of
+// the shape (the fused epilogue exists only in the RBULK kernel).
+constexpr int kAllreduceFallbacks[] = {87, 85, 82};
+
 int dispatch_allreduce(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
+    int rc = dispatch_allreduce_one(id, p, tp, s, pdl);
+    if (rc != SWB_E_UNSUPPORTED) return rc;
+    for (int alt : kAllreduceFallbacks) {
+        if (alt == id) continue;
+        rc = dispatch_allreduce_one(alt, p, tp, s, pdl);
+        if (rc != SWB_E_UNSUPPORTED) return rc;
+    }
+    return rc;
+}
+
+int dispatch_allreduce_one(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
     switch (id) {
 #define SWB_AR_CASE(ID, FAM, W, R, PK, U, CH, ST) \
     case ID:                                      \

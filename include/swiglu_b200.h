@@ -155,7 +155,8 @@ SWB_API int swb_tp_ipc_handle(const swb_tp_t* tp, void* out);
 SWB_API int swb_tp_connect(swb_tp_t* tp, const void* handles);
 SWB_API int swb_tp_destroy(swb_tp_t* tp);
 /* One rank's whole layer: gate on its shard, then the fused down + all-reduce;
- * y: [hidden] fp32, identical on every rank. down_config must be an RBULK id. */
+ * y: [hidden] fp32, identical on every rank. down_config must be an RBULK id;
+ * when its rows cannot hold the shard's columns, RBULK 87, 85 or 82 runs instead. */
 SWB_API int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard,
                              const void* wu_shard, const void* wd_shard, const void* x, const void* bg_shard,
                              const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,
