@@ -146,7 +146,8 @@ def tune(torch, binding, launch_gate, launch_down, ids, stream, reps=8, down_ids
 
 
 def traffic_from_profile(kernel_tag: str, H: int, I: int):
-    """DRAM bytes per launch recorded by the committed ncu summary for this kernel/workload, if any."""
+    """DRAM bytes per launch recorded by the committed ncu summary for this kernel/workload, if any
+    (the gate stage of a layer H -> I; a tensor-parallel shard's launch is that figure over N)."""
     path = ROOT / "profiles" / f"{kernel_tag}_{H}x{I}.txt"
     try:
         for line in path.read_text().splitlines():
@@ -390,7 +391,9 @@ def ours(args) -> None:
     roofline = {"bound": "hbm", "kernel": f"gate (config {gcfg})", "achieved": achieved, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "peak_source": f"{peaks['source']} copy bandwidth",
-                "traffic": traffic_from_profile("gate", H, shard), "bytes_per_launch": gate_bytes,
+                "traffic": (lambda t: None if t is None else t // world)(traffic_from_profile("gate", H, I)),
+                "traffic_source": "profiles/gate_%dx%d.txt (ncu, full layer; scaled by 1/N for a shard)" % (H, I),
+                "bytes_per_launch": gate_bytes,
                 "launch_us": gate_us}
     layer_gbs = rank_bytes / (us_per_layer * 1e-6) / 1e9
     layer_roofline = {"achieved": layer_gbs, "frac": layer_gbs / peaks["hbm_gbs"], "unit": "GB/s",
