@@ -83,3 +83,16 @@
 // Ids used when a BULK / RBULK geometry cannot run a shape.
 #define SWB_BULK_FALLBACK_ID 33
 #define SWB_RBULK_FALLBACK_ID 64
+
+// Fused whole-layer kernels (layer.cuh), used by swb_ffn_fused and, with a layer
+// id as the gate config, swb_ffn_tp_fused. Separate ids (200+): they run a whole
+// layer, not one projection. X(id, consumer warps, CTAs per SM, target bytes per
+// ring stage, maximum ring depth). The first two are the fallbacks, in order,
+// when a requested geometry cannot hold a row of the shape.
+#define SWB_LAYER_CONFIGS(X)    \
+    X(200, 8, 1, 32768, 8)      \
+    X(203, 16, 1, 32768, 8)     \
+    X(201, 4, 2, 32768, 4)      \
+    X(202, 8, 2, 16384, 8)      \
+    X(204, 4, 2, 16384, 8)      \
+    X(205, 8, 1, 16384, 12)

@@ -16,6 +16,7 @@
 #include <string>
 
 #include "kernels.cuh"
+#include "layer.cuh"
 #include "registry.h"
 #include "swiglu_b200.h"
 
@@ -400,6 +401,86 @@ int dispatch_fallback(int64_t id, Params p, cudaStream_t stream, bool pdl) {
     return dispatch<MODE>(id, p, stream, pdl);
 }
 
+// ---------------------------------------------------------------- layer
+template <int CW, int CPS, int TARGET, int ST, bool TP>
+int launch_layer(LayerParams L, const TpParams& tp, cudaStream_t stream) {
+    static std::atomic<uint64_t> smem_set{0};
+    constexpr int CT = CW * 32;
+    const bool ok = L.hidden % 8 == 0 && L.inter % 8 == 0 && (reinterpret_cast<uintptr_t>(L.wg) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(L.wu) % 16) == 0 && (reinterpret_cast<uintptr_t>(L.wd) % 16) == 0 &&
+                    L.hidden / 8 <= kLayerMaxJ * CT && L.inter / 8 <= kLayerMaxJ * CT;
+    if (!ok) return fail(SWB_E_UNSUPPORTED, "layer geometry cannot hold a row of this shape");
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const int G = std::min({sms * CPS, L.inter, L.hidden});
+    if (G > kLayerMaxCtas || G > kTpMaxCtas) return fail(SWB_E_UNSUPPORTED, "grid larger than the barrier table");
+    const size_t row1 = size_t(4) * L.hidden, row2 = size_t(2) * L.inter;
+    const size_t stage = align_up(std::max<size_t>({size_t(TARGET), row1, row2}), 16);
+    const int rpc1 = (L.inter + G - 1) / G, rpc2 = (L.hidden + G - 1) / G;
+    const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
+    int stages = ST;
+    while (stages >= 2 && layer_layout(int(stage), stages, CW, rpc1, rpc2).total > budget) --stages;
+    if (stages < 2) return fail(SWB_E_UNSUPPORTED, "layer does not fit the geometry's shared memory");
+    L.stage_bytes = int(stage);
+    L.stages = stages;
+    L.rs1 = std::max(1, std::min(int(stage / row1), rpc1));
+    L.rs2 = std::max(1, std::min(int(stage / row2), rpc2));
+    const size_t smem = layer_layout(L.stage_bytes, stages, CW, rpc1, rpc2).total;
+    auto kernel = layer_kernel<CW, CPS, TP>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    // The grid barrier needs every CTA resident at once: a cooperative launch
+    // makes the runtime check that instead of leaving it to chance.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(G));
+    cfg.blockDim = dim3((CW + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, L, tp);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    }
+    return check_launch();
+}
+
+constexpr int kLayerIds[] = {
+#define SWB_LAYER_ID(ID, CW, CPS, TGT, ST) ID,
+    SWB_LAYER_CONFIGS(SWB_LAYER_ID)
+#undef SWB_LAYER_ID
+};
+
+bool is_layer_config(int64_t id) {
+    for (int v : kLayerIds)
+        if (v == id) return true;
+    return false;
+}
+
+template <bool TP>
+int dispatch_layer_one(int64_t id, const LayerParams& L, const TpParams& tp, cudaStream_t s) {
+    switch (id) {
+#define SWB_LAYER_CASE(ID, CW, CPS, TGT, ST) \
+    case ID:                                 \
+        return launch_layer<CW, CPS, TGT, ST, TP>(L, tp, s);
+        SWB_LAYER_CONFIGS(SWB_LAYER_CASE)
+#undef SWB_LAYER_CASE
+        default:
+            return fail(SWB_E_CONFIG);
+    }
+}
+
+template <bool TP>
+int dispatch_layer(int64_t id, const LayerParams& L, const TpParams& tp, cudaStream_t s) {
+    int rc = dispatch_layer_one<TP>(id, L, tp, s);
+    for (int i = 0; i < 2 && rc == SWB_E_UNSUPPORTED; ++i)
+        if (kLayerIds[i] != id) rc = dispatch_layer_one<TP>(kLayerIds[i], L, tp, s);
+    return rc;
+}
+
 bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {
     const uintptr_t ap = reinterpret_cast<uintptr_t>(a), bp = reinterpret_cast<uintptr_t>(b);
     return ap < bp + bbytes && bp < ap + abytes;
@@ -663,7 +744,7 @@ int swb_tp_create(int rank, int world, int rows, swb_tp_t** out) {
     tp->rows = rows;
     tp->recv_bytes = tp_recv_bytes(world, rows);
     tp->flag_bytes = tp_flag_bytes(world);
-    tp->bytes = tp->recv_bytes + tp->flag_bytes + align_up(size_t(kTpMaxCtas) * 4, 256);
+    tp->bytes = tp->recv_bytes + tp->flag_bytes + align_up(size_t(kTpMaxCtas) * 4, 256) + SWB_LAYER_WORKSPACE_BYTES;
     cudaError_t e = cudaGetDevice(&tp->device);
     if (e == cudaSuccess) e = cudaMalloc(&tp->local, tp->bytes);  // set-up time, once per rank
     if (e == cudaSuccess) e = cudaMemset(tp->local, 0, tp->bytes);
@@ -720,9 +801,41 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
                      void* h_shard, float* y, int hidden, int shard, void* stream) {
     if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
     if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
-    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
+    const bool layer = is_layer_config(gate_config);
+    if (!layer && (!find_config(gate_config) || !find_config(down_config))) return fail(SWB_E_CONFIG);
     if (!wd_shard || !x) return fail(SWB_E_INPUT);
     if (!y) return fail(SWB_E_FLOAT_OUTPUT);
+    if (layer) {  // one persistent kernel: gate, grid barrier, down + exchange
+        if (!wg_shard || !wu_shard || !h_shard) return fail(SWB_E_GATE_BUFFERS);
+        LayerParams L;
+        std::memset(&L, 0, sizeof L);
+        L.wg = static_cast<const __half*>(wg_shard);
+        L.wu = static_cast<const __half*>(wu_shard);
+        L.wd = static_cast<const __half*>(wd_shard);
+        L.x = static_cast<const __half*>(x);
+        L.bg = static_cast<const __half*>(bg_shard);
+        L.bu = static_cast<const __half*>(bu_shard);
+        L.h = static_cast<__half*>(h_shard);
+        L.y = y;
+        L.hidden = hidden;
+        L.inter = shard;
+        char* base = static_cast<char*>(tp->local);
+        L.sync = reinterpret_cast<uint32_t*>(base + tp->recv_bytes + tp->flag_bytes +
+                                             align_up(size_t(kTpMaxCtas) * 4, 256));
+        TpParams t;
+        std::memset(&t, 0, sizeof t);
+        for (int q = 0; q < tp->world; ++q) {
+            char* pb = static_cast<char*>(tp->peer[q]);
+            t.recv[q] = reinterpret_cast<float*>(pb);
+            t.flags[q] = reinterpret_cast<uint32_t*>(pb + tp->recv_bytes);
+        }
+        t.ctr = reinterpret_cast<uint32_t*>(base + tp->recv_bytes + tp->flag_bytes);
+        t.bias = static_cast<const __half*>(bd);
+        t.residual = static_cast<const __half*>(x);
+        t.rank = tp->rank;
+        t.world = tp->world;
+        return dispatch_layer<true>(gate_config, L, t, static_cast<cudaStream_t>(stream));
+    }
     if (int rc = swb_gate(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream))
         return rc;
     Params p = make_params();
@@ -744,6 +857,46 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
     t.rank = tp->rank;
     t.world = tp->world;
     return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int swb_layer_config_count(void) { return int(sizeof(kLayerIds) / sizeof(kLayerIds[0])); }
+
+int swb_layer_config_ids(int* out, int cap) {
+    const int n = swb_layer_config_count();
+    if (out)
+        for (int i = 0; i < n && i < cap; ++i) out[i] = kLayerIds[i];
+    return n;
+}
+
+int swb_ffn_fused(int layer_config, const void* wg, const void* wu, const void* wd, const void* x, const void* bg,
+                  const void* bu, const void* bd, void* h, float* y, int hidden, int inter, void* workspace,
+                  void* stream) {
+    if (!is_layer_config(layer_config)) return fail(SWB_E_CONFIG);
+    if (hidden <= 0 || inter <= 0 || !wg || !x || !wd) return fail(SWB_E_INPUT);
+    if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
+    if (!y) return fail(SWB_E_FLOAT_OUTPUT);
+    if (!workspace) return fail(SWB_E_WORKSPACE, "swb_ffn_fused needs its SWB_LAYER_WORKSPACE_BYTES workspace");
+    LayerParams L;
+    std::memset(&L, 0, sizeof L);
+    L.wg = static_cast<const __half*>(wg);
+    L.wu = static_cast<const __half*>(wu);
+    L.wd = static_cast<const __half*>(wd);
+    L.x = static_cast<const __half*>(x);
+    L.bg = static_cast<const __half*>(bg);
+    L.bu = static_cast<const __half*>(bu);
+    L.bd = static_cast<const __half*>(bd);
+    L.h = static_cast<__half*>(h);
+    L.y = y;
+    L.sync = static_cast<uint32_t*>(workspace);
+    L.hidden = hidden;
+    L.inter = inter;
+    TpParams t;
+    std::memset(&t, 0, sizeof t);
+    return dispatch_layer<false>(layer_config, L, t, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -38,6 +38,7 @@ SWB_E_UNSUPPORTED = 14
 SWB_E_WORKSPACE = 15
 SWB_NOALLOC_MAX_INTER = 65536
 SWB_TP_MAX_RANKS = 8
+SWB_LAYER_WORKSPACE_BYTES = 8192
 SWB_TP_HANDLE_BYTES = 64
 SWB_DEVERR_PEER_TIMEOUT = 2
 SWB_RESIDUAL = 1
@@ -91,6 +92,9 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_ffn": ([_i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
         "swb_ffn_tp": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_ffn_noalloc": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
+        "swb_layer_config_count": ([], _i),
+        "swb_layer_config_ids": ([ctypes.POINTER(_i), _i], _i),
+        "swb_ffn_fused": ([_i] + [_vp] * 9 + [_i, _i, _vp, _vp], _i),
         "swb_swiglu_out": ([_vp] * 6 + [_i64] * 4 + [_vp], _i),
         "swb_tp_create": ([_i, _i, _i, ctypes.POINTER(_vp)], _i),
         "swb_tp_ipc_handle": ([_vp, _vp], _i),

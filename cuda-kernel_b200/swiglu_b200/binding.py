@@ -141,6 +141,32 @@ def ffn(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, b
                                       y.data_ptr(), hidden, inter, s))
 
 
+def layer_config_ids() -> list[int]:
+    """Ids of the fused whole-layer kernels (swb_ffn_fused)."""
+    L = _lib.lib()
+    n = L.swb_layer_config_count()
+    buf = (_lib.ctypes.c_int * n)()
+    L.swb_layer_config_ids(buf, n)
+    return list(buf)
+
+
+def layer_workspace(device: torch.device | int | None = None) -> torch.Tensor:
+    """A zeroed workspace for swb_ffn_fused (one per stream of calls)."""
+    return torch.zeros(_lib.SWB_LAYER_WORKSPACE_BYTES, dtype=torch.uint8, device=device or "cuda")
+
+
+def ffn_fused(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, bg: torch.Tensor,
+              bu: torch.Tensor, bd: torch.Tensor, h: torch.Tensor, y: torch.Tensor, layer_config: int,
+              workspace: torch.Tensor, stream: int | None = None) -> None:
+    """The whole layer as one persistent kernel (gate, grid barrier, down): y fp32 [H]."""
+    inter, hidden = wg.shape
+    s = _stream(x.device) if stream is None else stream
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().swb_ffn_fused(int(layer_config), wg.data_ptr(), wu.data_ptr(), wd.data_ptr(),
+                                            x.data_ptr(), _ptr(bg), _ptr(bu), _ptr(bd), h.data_ptr(), y.data_ptr(),
+                                            hidden, inter, workspace.data_ptr(), s))
+
+
 def ffn_tp(x: torch.Tensor, wg_shard: torch.Tensor, wu_shard: torch.Tensor, wd_shard: torch.Tensor,
            bg_shard: torch.Tensor | None, bu_shard: torch.Tensor | None, h_shard: torch.Tensor,
            y_partial: torch.Tensor, gate_config: int, down_config: int, stream: int | None = None) -> None:

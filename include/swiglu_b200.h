@@ -124,6 +124,22 @@ SWB_API int swb_ffn_noalloc(int gate_config, int down_config, const void* wg, co
                             const void* x, const void* bg, const void* bu, const void* bd, float* y, int hidden,
                             int inter, void* stream);
 
+/* The whole layer in ONE persistent kernel (no counterpart in the reference): gate
+ * rows, a grid barrier, then down rows, with the weight stream running straight
+ * from Wg/Wu into Wd. Same arguments and outputs as swb_ffn plus `workspace`:
+ * SWB_LAYER_WORKSPACE_BYTES of device memory, zeroed once when allocated, then
+ * reused by every call on one stream (calls sharing a workspace must not overlap).
+ * layer_config is a layer id (swb_layer_config_ids); a geometry that cannot hold
+ * a row of the shape falls back to 200, then 203. Needs hidden and inter
+ * multiples of 8 and 16-byte aligned weights (else SWB_E_UNSUPPORTED: use swb_ffn).
+ * The launch is cooperative: every CTA must be resident at once. */
+#define SWB_LAYER_WORKSPACE_BYTES 8192
+SWB_API int swb_layer_config_count(void);
+SWB_API int swb_layer_config_ids(int* out, int cap);
+SWB_API int swb_ffn_fused(int layer_config, const void* wg, const void* wu, const void* wd, const void* x,
+                          const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
+                          void* workspace, void* stream);
+
 /* Tensor-parallel rank of the layer (no counterpart in the reference, which is
  * single-GPU; it splits benchmark.cu:161-165 n ways). wg_shard, wu_shard: rows
  * [r*inter/n, (r+1)*inter/n) of Wg, Wu -> [shard, hidden]; wd_shard: the matching
@@ -156,7 +172,9 @@ SWB_API int swb_tp_connect(swb_tp_t* tp, const void* handles);
 SWB_API int swb_tp_destroy(swb_tp_t* tp);
 /* One rank's whole layer: gate on its shard, then the fused down + all-reduce;
  * y: [hidden] fp32, identical on every rank. down_config must be an RBULK id;
- * when its rows cannot hold the shard's columns, RBULK 87, 85 or 82 runs instead. */
+ * when its rows cannot hold the shard's columns, RBULK 87, 85 or 82 runs instead.
+ * With a layer id (swb_layer_config_ids) as gate_config the rank's whole layer,
+ * exchange included, is one persistent kernel and down_config is ignored. */
 SWB_API int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard,
                              const void* wu_shard, const void* wd_shard, const void* x, const void* bg_shard,
                              const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,

@@ -172,3 +172,15 @@ def test_ctypes_declarations_match_header_arity():
         fn = getattr(_lib.cublas_lib() if name.startswith("swbl_") else L(), name)
         assert fn.argtypes is not None, name
         assert len(fn.argtypes) == nparams, (name, len(fn.argtypes), nparams)
+
+
+def test_layer_registry_and_fused_guards():
+    from swiglu_b200 import layer_config_ids
+    ids = layer_config_ids()
+    assert ids[:2] == [200, 203] and all(i >= 200 for i in ids)
+    assert not set(ids) & set(__import__("swiglu_b200").config_ids())
+    f = L().swb_ffn_fused
+    assert f(33, *([FAKE] * 9), 64, 96, FAKE, None) == _lib.SWB_E_CONFIG        # projection id, not a layer id
+    assert f(200, *([FAKE] * 9), 64, 96, None, None) == _lib.SWB_E_WORKSPACE
+    assert f(200, None, *([FAKE] * 8), 64, 96, FAKE, None) == _lib.SWB_E_INPUT
+    assert f(200, FAKE, None, *([FAKE] * 7), 64, 96, FAKE, None) == _lib.SWB_E_GATE_BUFFERS

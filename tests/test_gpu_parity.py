@@ -265,3 +265,49 @@ def test_cublas_baseline_matches_oracle():
         assert O.compare(y.cpu().numpy(), case.y)[0]
         assert rel_err(h.cpu().numpy(), case.act) <= H_TOL
     base.close()
+
+
+# ---- the fused whole-layer kernel (one persistent launch) --------------------
+
+@pytest.mark.parametrize("shape", [(4096, 14336), (4096, 11008), (2048, 8192), (2048, 5632), (512, 1376),
+                                   (64, 96), (1024, 256)])
+def test_fused_layer_kernel_matches_oracle(shape):
+    case = Case(*shape)
+    d = case.d
+    ws = binding.layer_workspace()
+    for cfg in binding.layer_config_ids():
+        for _ in range(2):  # the launch epoch advances call after call
+            h = torch.empty(case.inter, dtype=torch.float16, device="cuda")
+            y = torch.empty(case.hidden, dtype=torch.float32, device="cuda")
+            binding.ffn_fused(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, cfg, ws)
+            assert rel_err(h.cpu().numpy(), case.act) <= H_TOL, cfg
+            yc = y.cpu().numpy()
+            assert rel_err(yc, case.y, case.y_atol) <= Y_TOL, cfg
+            assert O.compare(yc, case.y)[0], cfg
+    assert binding.device_error() == 0
+
+
+def test_fused_layer_in_cuda_graph_and_unsupported_shapes():
+    case = Case(2048, 5632)
+    d = case.d
+    ws = binding.layer_workspace()
+    h = torch.empty(case.inter, dtype=torch.float16, device="cuda")
+    y = torch.empty(case.hidden, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        binding.ffn_fused(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, 200, ws)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            binding.ffn_fused(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, 200, ws)
+        for _ in range(4):
+            y.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert rel_err(y.cpu().numpy(), case.y, case.y_atol) <= Y_TOL
+        g.reset()
+    odd = Case(2047, 5631)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        binding.ffn_fused(odd.d["x"], odd.d["wg"], odd.d["wu"], odd.d["wd"], odd.d["bg"], odd.d["bu"], odd.d["bd"],
+                          torch.empty(5631, dtype=torch.float16, device="cuda"),
+                          torch.empty(2047, dtype=torch.float32, device="cuda"), 200, ws)
+    assert binding.device_error() == 0

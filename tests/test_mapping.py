@@ -403,3 +403,58 @@ def test_sbulk_blocks_leave_work_to_steal(configs):
             plan = sbulk_plan(cfg, rows, cols, gated)
             if plan is not None:
                 assert plan["blocks"] >= 4 * SMS * cfg["rows"], (cfg["id"], plan)
+
+
+LAYER_GEOMS = {200: (8, 1, 32768, 8), 203: (16, 1, 32768, 8), 201: (4, 2, 32768, 4), 202: (8, 2, 16384, 8),
+               204: (4, 2, 16384, 8), 205: (8, 1, 16384, 12)}
+
+
+def layer_plan(cfg_id, hidden, inter):
+    """Mirror of launch_layer (csrc/swiglu_b200.cu)."""
+    cw, cps, target, smax = LAYER_GEOMS[cfg_id]
+    ct = cw * 32
+    if hidden % 8 or inter % 8 or hidden // 8 > 8 * ct or inter // 8 > 8 * ct:
+        return None
+    G = min(SMS * cps, inter, hidden)
+    row1, row2 = 4 * hidden, 2 * inter
+    stage = -(-max(target, row1, row2) // 16) * 16
+    rpc1, rpc2 = -(-inter // G), -(-hidden // G)
+    budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 128
+
+    def total(stages):
+        up = lambda v, a: -(-v // a) * a  # noqa: E731
+        full = up(stages * stage, 16)
+        part1 = up(full + 16 * stages, 16)
+        part2 = up(part1 + rpc1 * cw * 8, 16)
+        return up(part2 + rpc2 * cw * 4, 16)
+    stages = smax
+    while stages >= 2 and total(stages) > budget:
+        stages -= 1
+    if stages < 2:
+        return None
+    return {"G": G, "stage": stage, "stages": stages, "rs1": max(1, min(stage // row1, rpc1)),
+            "rs2": max(1, min(stage // row2, rpc2)), "total": total(stages), "budget": budget}
+
+
+def test_layer_kernel_plans_cover_both_phases():
+    assert layer_plan(200, 2047, 5631) is None
+    for hidden, inter in ((4096, 14336), (4096, 11008), (2048, 8192), (2048, 5632), (512, 1376), (64, 96),
+                          (4096, 7168), (4096, 3584), (4096, 1792), (1024, 256)):
+        plans = {c: layer_plan(c, hidden, inter) for c in LAYER_GEOMS}
+        assert plans[200] is not None or plans[203] is not None, (hidden, inter)
+        for c, plan in plans.items():
+            if plan is None:
+                continue
+            assert plan["total"] <= plan["budget"] and plan["G"] <= 1024
+            assert plan["rs1"] * 4 * hidden <= plan["stage"] and plan["rs2"] * 2 * inter <= plan["stage"]
+            for rows, cols, rs, nm in ((inter, hidden, plan["rs1"], 2), (hidden, inter, plan["rs2"], 1)):
+                owner = np.zeros(rows, np.int64)
+                for b in range(plan["G"]):
+                    r0, r1 = b * rows // plan["G"], (b + 1) * rows // plan["G"]
+                    assert r1 > r0
+                    for row in range(r0, r1, rs):
+                        ru = min(rs, r1 - row)
+                        assert (ru * cols * 2) % 16 == 0 and (row * cols * 2) % 16 == 0
+                        assert nm * ru * cols * 2 < (1 << 20)
+                        owner[row:row + ru] += 1
+                assert (owner == 1).all()

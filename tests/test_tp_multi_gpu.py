@@ -64,9 +64,9 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
     from swiglu_b200 import tp as T
     ex = T.Exchange(rank, world, hidden, dev)
     s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
-    for down in (80, 83, 87, 87, 87):
+    for gate, down in ((69, 80), (69, 83), (69, 87), (69, 87), (200, 0), (201, 0), (200, 0)):
         y.zero_()
-        T.ffn_tp_fused(ex, x, s, bd, h, y, 69, down)
+        T.ffn_tp_fused(ex, x, s, bd, h, y, gate, down)  # 200+: the rank's whole layer in one kernel
         torch.cuda.synchronize()
         out.append(y.cpu().numpy().copy())
     dist.barrier()
