@@ -1,10 +1,18 @@
 """GPU parity: every registry geometry against the CPU oracle, through the C ABI.
 
 Tolerances (stated here, checked per element), relative error |a - e| / (|e| + atol):
-* fp16 h: atol = 1e-3 * max|h|, bound 1e-2;
-* fp32 y: atol_j = 2^-11 * sum_i |Wd[j,i] * h[i]| -- the largest change one fp16
-  rounding of h can make in y_j (h is an fp16 intermediate by contract) -- bound 2e-3;
-* and the reference's own gate (include/contract.hpp:36-53): atol 0.003, rtol 0.01.
+* fp16 h against the oracle's h: atol = 1e-3 * max|h|, bound 1e-2; every element
+  within one fp16 ulp plus the fp32 summation bound carried through the
+  activation, |dh/dg| * K * 2^-24 * sum|Wg x| + |dh/du| * K * 2^-24 * sum|Wu x|;
+  and at most 2% of the elements with other bits (the GPU sums in fp32, the oracle
+  in double, so a value near an fp16 rounding midpoint can round the other way;
+  truncating instead of rounding to nearest would change about half);
+* fp32 y against the oracle's down projection of the GPU's own h:
+  atol_j = 2^-11 * sum_i |Wd[j,i] * h[i]|, bound 2e-3 (checking y against the
+  oracle's h instead would charge one flipped h element, |Wd[j,i]| * ulp(h_i), to
+  every row j);
+* and y against the full oracle with the reference's own gate
+  (include/contract.hpp:36-53): atol 0.003, rtol 0.01.
 The model-rounding binding path is checked as tools/gpu_validate.py checks it
 (torch fp16 reference, atol .01, rtol .02) and against the oracle's fp16 path.
 """
@@ -38,6 +46,41 @@ def rel_err(actual, expected, atol=None):
 def y_atol(wd, h):
     """Per-row error scale of y from one fp16 rounding of h: 2^-11 * sum_i |Wd[j,i] h[i]|."""
     return 2.0 ** -11 * (np.abs(wd.astype(np.float32)) @ np.abs(h.astype(np.float32))).astype(np.float64)
+
+
+def h_bound(w, e):
+    """One fp16 ulp of the oracle's h plus the fp32 summation bound carried through silu(g) * u."""
+    f = lambda a: O.f16_values(a).astype(np.float64)  # noqa: E731
+    x = f(w["x"])
+    wg, wu = f(w["wg"]), f(w["wu"])
+    g, u = wg @ x + f(w["bg"]), wu @ x + f(w["bu"])
+    gamma = x.size * 2.0 ** -24
+    sig = 1.0 / (1.0 + np.exp(-g))
+    dg = np.abs(sig * (1 + g * (1 - sig)) * u)  # d(silu(g) u)/dg
+    return (np.spacing(np.abs(e)).astype(np.float64) + 1e-12
+            + gamma * (dg * (np.abs(wg) @ np.abs(x)) + np.abs(g * sig) * (np.abs(wu) @ np.abs(x))))
+
+
+def check_h_close(h, case):
+    """Per-element bound (one ulp + fp32 summation error), at most 2% of bits off, and the relative bound."""
+    h = np.asarray(h, np.float16)
+    e = np.asarray(case.act, np.float16)
+    assert np.isfinite(h.astype(np.float32)).all()
+    if getattr(case, "_h_bound", None) is None:
+        case._h_bound = h_bound(case.w, e)
+    bound = case._h_bound
+    diff = np.abs(h.astype(np.float64) - e.astype(np.float64))
+    assert (diff <= bound).all(), int(np.argmax(diff - bound))
+    assert np.mean(h.view(np.uint16) != e.view(np.uint16)) <= 0.02
+    assert rel_err(h, e) <= H_TOL
+
+
+def check_y_given_h(w, h_gpu, y_gpu, y_full):
+    """y against the oracle's down projection of the GPU's h, then against the full oracle (reference gate)."""
+    h16 = np.asarray(h_gpu, np.float16)
+    y_own = O.project(w["wd"], h16, w["bd"], w["x"])
+    assert rel_err(y_gpu, y_own, y_atol(w["wd"], h16)) <= Y_TOL
+    assert O.compare(y_gpu, y_full)[0]
 
 
 def dev(a, offset=0):
@@ -77,9 +120,7 @@ class Case:
 
 
 def check_gate(case, h):
-    h = h.cpu().numpy()
-    assert np.isfinite(h).all()
-    assert rel_err(h, case.act) <= H_TOL
+    check_h_close(h.cpu().numpy(), case)
 
 
 def check_down(case, y):
@@ -131,10 +172,9 @@ def test_full_layer_matches_reference_oracle(shape, ids):
         h = torch.empty(case.inter, dtype=torch.float16, device="cuda")
         y = torch.empty(case.hidden, dtype=torch.float32, device="cuda")
         binding.ffn(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, g, dd)
-        assert rel_err(h.cpu().numpy(), case.act) <= H_TOL, (g, dd)
-        yc = y.cpu().numpy()
-        assert rel_err(yc, case.y, case.y_atol) <= Y_TOL, (g, dd)
-        assert O.compare(yc, case.y)[0], (g, dd)
+        hc = h.cpu().numpy()
+        check_h_close(hc, case)
+        check_y_given_h(case.w, hc, y.cpu().numpy(), case.y)
 
 
 def test_reference_golden_uniform_workload(ids):
@@ -280,10 +320,9 @@ def test_fused_layer_kernel_matches_oracle(shape):
             h = torch.empty(case.inter, dtype=torch.float16, device="cuda")
             y = torch.empty(case.hidden, dtype=torch.float32, device="cuda")
             binding.ffn_fused(d["x"], d["wg"], d["wu"], d["wd"], d["bg"], d["bu"], d["bd"], h, y, cfg, ws)
-            assert rel_err(h.cpu().numpy(), case.act) <= H_TOL, cfg
-            yc = y.cpu().numpy()
-            assert rel_err(yc, case.y, case.y_atol) <= Y_TOL, cfg
-            assert O.compare(yc, case.y)[0], cfg
+            hc = h.cpu().numpy()
+            check_h_close(hc, case)
+            check_y_given_h(case.w, hc, y.cpu().numpy(), case.y)
     assert binding.device_error() == 0
 
 
@@ -303,7 +342,7 @@ def test_fused_layer_in_cuda_graph_and_unsupported_shapes():
             y.zero_()
             g.replay()
             torch.cuda.synchronize()
-            assert rel_err(y.cpu().numpy(), case.y, case.y_atol) <= Y_TOL
+            check_y_given_h(case.w, h.cpu().numpy(), y.cpu().numpy(), case.y)
         g.reset()
     odd = Case(2047, 5631)
     with pytest.raises(RuntimeError, match="unsupported"):
