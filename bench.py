@@ -6,7 +6,9 @@ y = Wd h + bd + x; fp16 weights, fp32 accumulation, fp16 h, fp32 y) on seeded
 synthetic inputs, weights cycling through rotating copies whose total exceeds
 twice the 126 MB L2, so every step streams its weights from HBM.
 
-* N = 1: the two product kernels (gate, down) on one B200.
+* N = 1: the layer on one B200, as whichever is faster on this GPU: the two
+  product kernels (gate, then down launched programmatically), or the whole
+  layer in one persistent kernel (gate, grid barrier, down).
 * N > 1 (torchrun, one rank per GPU): tensor parallel. Wg/Wu split by
   intermediate row, Wd by its K dimension; the down kernel sums the ranks'
   partial y over NVLink peer memory and adds bias + residual once (fused
@@ -46,6 +48,8 @@ def parse():
     p.add_argument("--intermediate", type=int, default=14336)
     p.add_argument("--gate-config", type=int, default=0, help="registry id (0 = tune)")
     p.add_argument("--down-config", type=int, default=0, help="registry id (0 = tune)")
+    p.add_argument("--layer-config", type=int, default=0,
+                   help="fused whole-layer kernel id (0 = tune against the two-kernel path, -1 = never)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-cublas", action="store_true")
@@ -273,19 +277,48 @@ def ours(args) -> None:
     if world > 1:
         from swiglu_b200.tp import Exchange
         exchange = Exchange(rank, world, H, device)  # one-time set-up: IPC handles shared by all_gather
+    workspace = binding.layer_workspace(device)  # grid-barrier slots of the one-GPU fused layer kernel
 
-    def step(i):
-        # the layer entry points: gate kernel, then the down kernel launched programmatically;
-        # for N > 1 the down kernel also sums the ranks' partials over NVLink (fused all-reduce)
+    def layer_step(cfg, g, d, i):
+        # cfg = 0: gate kernel, then the down kernel launched programmatically (for N > 1 the
+        # down kernel also sums the ranks' partials over NVLink); cfg > 0: the whole layer
+        # (and, for N > 1, the exchange) in one persistent kernel
         s = sets[i % copies]
-        if world == 1:
-            _lib.check(L.swb_ffn(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+        if world == 1 and cfg:
+            _lib.check(L.swb_ffn_fused(cfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                       x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
+                                       y.data_ptr(), H, shard, workspace.data_ptr(), sp))
+        elif world == 1:
+            _lib.check(L.swb_ffn(g, d, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
                                  x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
                                  y.data_ptr(), H, shard, sp))
         else:
-            _lib.check(L.swb_ffn_tp_fused(exchange.handle, gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(),
-                                          s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(), bu.data_ptr(),
-                                          bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard, sp))
+            _lib.check(L.swb_ffn_tp_fused(exchange.handle, cfg or g, 0 if cfg else d, s["wg"].data_ptr(),
+                                          s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(),
+                                          bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard, sp))
+
+    # the fused whole-layer kernels against the tuned two-kernel step, timed the same way
+    # (every rank times the same candidates in the same order; rank 0's choice is broadcast)
+    lcfg = max(args.layer_config, 0)
+    layer_times = {}
+    if args.layer_config == 0:
+        cands = [0] + binding.layer_config_ids()
+        for c in cands:
+            try:
+                layer_step(c, gcfg, dcfg, 0)
+            except RuntimeError:  # geometry does not hold this shape (same answer on every rank)
+                continue
+            torch.cuda.synchronize()
+            samples = [time_kernel(torch, lambda i, c=c: layer_step(c, gcfg, dcfg, i), 8, stream) for _ in range(3)]
+            layer_times[c] = statistics.median(samples)
+        lcfg = min(layer_times, key=layer_times.get)
+        if world > 1:
+            t = torch.tensor([lcfg], dtype=torch.int64, device=device)
+            dist.broadcast(t, 0)
+            lcfg = int(t[0])
+
+    def step(i):
+        layer_step(lcfg, gcfg, dcfg, i)
 
     def step_nccl(i):
         # the baseline tensor-parallel step: partial y, NCCL all-reduce, then bias + residual
@@ -322,7 +355,7 @@ def ours(args) -> None:
         dist.all_reduce(dn, op=dist.ReduceOp.MAX)
         if not float(dn) <= 1e-5:
             raise SystemExit(f"fused and NCCL tensor-parallel paths disagree: {float(dn)}")
-    launches_per_step = 2
+    launches_per_step = 1 if lcfg else 2
 
     # ---- one CUDA graph per rotating copy holds the whole step (as the reference
     # times its candidates: src/benchmark.cu:46-83); for N > 1 it includes the NCCL all-reduce
@@ -375,26 +408,35 @@ def ours(args) -> None:
             dist.barrier()
     us_per_layer = elapsed_ms * 1e3 / args.steps
 
-    # ---- dominant kernel (gate): CUDA events around each launch, same rotating copies
-    gate_events = []
+    # ---- dominant kernel: CUDA events around each launch, same rotating copies. With the
+    # fused layer kernel that is the one launch of the step; otherwise the gate kernel.
+    events = []
     for i in range(args.steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        launch_gate(gcfg, i)
-        b.record(stream)
-        launch_down(dcfg, i)
-        gate_events.append((a, b))
+        if lcfg:
+            a.record(stream)
+            step(i)
+            b.record(stream)
+        else:
+            a.record(stream)
+            launch_gate(gcfg, i)
+            b.record(stream)
+            launch_down(dcfg, i)
+        events.append((a, b))
     torch.cuda.synchronize()
-    gate_us = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in gate_events)
+    launch_us = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in events)
     peaks = intensity.measured_peaks(ROOT / "MEASURED_PEAKS.json")
-    achieved = gate_bytes / (gate_us * 1e-6) / 1e9
-    roofline = {"bound": "hbm", "kernel": f"gate (config {gcfg})", "achieved": achieved, "peak": peaks["hbm_gbs"],
+    kbytes, ktag = (rank_bytes, "layer") if lcfg else (gate_bytes, "gate")
+    achieved = kbytes / (launch_us * 1e-6) / 1e9
+    kname = (f"fused layer (config {lcfg})" + (" with the NVLink exchange" if world > 1 else "")) if lcfg \
+        else f"gate (config {gcfg})"
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "peak_source": f"{peaks['source']} copy bandwidth",
-                "traffic": (lambda t: None if t is None else t // world)(traffic_from_profile("gate", H, I)),
-                "traffic_source": "profiles/gate_%dx%d.txt (ncu, full layer; scaled by 1/N for a shard)" % (H, I),
-                "bytes_per_launch": gate_bytes,
-                "launch_us": gate_us}
+                "traffic": (lambda t: None if t is None else t // world)(traffic_from_profile(ktag, H, I)),
+                "traffic_source": "profiles/%s_%dx%d.txt (ncu, full layer; scaled by 1/N for a shard)" % (ktag, H, I),
+                "bytes_per_launch": kbytes,
+                "launch_us": launch_us}
     layer_gbs = rank_bytes / (us_per_layer * 1e-6) / 1e9
     layer_roofline = {"achieved": layer_gbs, "frac": layer_gbs / peaks["hbm_gbs"], "unit": "GB/s",
                       "bytes_per_step_per_rank": rank_bytes}
@@ -467,14 +509,21 @@ def ours(args) -> None:
         y_host = torch.empty(H, dtype=torch.float32).pin_memory()
         x_dev = torch.empty_like(x)
         e2e_graphs = []
+        def public_call(c):
+            if lcfg:
+                binding.ffn_fused(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, lcfg,
+                                  workspace, stream=sp)
+            else:
+                binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg,
+                            stream=sp)
+
         for c in range(copies):
-            binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg, stream=sp)
+            public_call(c)
         torch.cuda.synchronize()
         for c in range(copies):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg,
-                            stream=sp)
+                public_call(c)
             e2e_graphs.append(g)
 
         def e2e_step(i):
@@ -491,7 +540,8 @@ def ours(args) -> None:
         e2e = {"value": e2e_us, "unit": UNIT,
                "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
-               "path": "pinned host x -> H2D -> captured swb_ffn (C ABI) -> D2H -> pinned host y"}
+               "path": "pinned host x -> H2D -> captured %s (C ABI) -> D2H -> pinned host y"
+                       % ("swb_ffn_fused" if lcfg else "swb_ffn")}
         del e2e_graphs
 
     # ---- cuBLAS GemmEx + pointwise on the same GPU (baseline, N=1)
@@ -539,6 +589,7 @@ def ours(args) -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
                        "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
+                       "layer_config": lcfg or None,
                        "rotating_copies": copies,
                        "l2": f"inputs larger than L2: {copies} rotating weight copies of "
                              f"{weight_bytes_rank / 2**20:.0f} MiB per rank",
@@ -550,6 +601,8 @@ def ours(args) -> None:
         if tuned is not None:
             line["tuning_us"] = {"gate": {str(k): round(v, 3) for k, v in tuned["gate_times"].items()},
                                  "down": {str(k): round(v, 3) for k, v in tuned["down_times"].items()}}
+        if layer_times:  # key 0 = the two-kernel step with the tuned gate/down pair
+            line.setdefault("tuning_us", {})["layer"] = {str(k): round(v, 3) for k, v in layer_times.items()}
         print(json.dumps(line), flush=True)
 
     # Release every graph (some hold NCCL all-reduces) before the process group goes.

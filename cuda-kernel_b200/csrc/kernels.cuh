@@ -642,8 +642,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
 
 // Tensor-parallel exchange of one layer call. Rank q's exchange buffer holds
 // recv[2][world][rows] fp32 (parity-double-buffered partials from every rank),
-// flags[world][kTpMaxCtas] (flags[src][cta] = call epoch of src's CTA) and this
-// rank's per-CTA call counters.
+// flags[world][kTpMaxCtas] (flags[src][cta] = the call epoch at which src's CTA
+// published) and this rank's call counter: ctr[0] = epoch of the last finished
+// exchange call, ctr[1] = CTAs of the running call that have finished.
 constexpr int kTpMaxRanks = 8;
 constexpr int kTpMaxCtas = 1024;
 
@@ -657,6 +658,22 @@ struct TpParams {
     int world;
 };
 
+// One epoch per exchange call, the same for every CTA whatever the grid: each CTA
+// reads it before it arrives, and the last CTA to arrive (on every exit path,
+// failures included) advances it, so the next call -- stream-ordered after this
+// one -- sees the new value. A per-CTA counter would not do: when consecutive
+// calls map rows to CTAs differently, a peer's CTA b could write this call's rows
+// into the parity buffer that another CTA here still reads for the previous call.
+__device__ __forceinline__ uint32_t tp_call_epoch(const TpParams& tp) {
+    return *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u;
+}
+
+__device__ __forceinline__ void tp_arrive(const TpParams& tp, uint32_t epoch) {
+    __threadfence();
+    if (atomicInc(tp.ctr + 1, gridDim.x - 1u) == gridDim.x - 1u)
+        *reinterpret_cast<volatile uint32_t*>(tp.ctr) = epoch;
+}
+
 // The down projection of a tensor-parallel rank with the all-reduce fused into
 // its epilogue. Every rank runs the same grid and row partition, so CTA b owns
 // rows [r0, r1) of y on every rank. CTA b: (1) stores its partial rows into
@@ -665,9 +682,9 @@ struct TpParams {
 // release; (3) waits (bounded) until every rank's CTA b has published epoch;
 // (4) sums the ranks' partials in rank order -- the same order on every rank, so
 // y is bit-identical everywhere -- adds bias + residual and writes y. The epoch
-// is CTA b's own call counter, so graph replays need no reset; a rank can run at
-// most one call ahead of a peer (it waits on that peer every call), which the
-// parity double buffer and the "reached" flag test cover.
+// lives in device memory (tp_call_epoch), so graph replays need no reset; a rank
+// can run at most one call ahead of a peer (it waits on that peer every call),
+// which the parity double buffer and the "reached" flag test cover.
 template <int CW, int MAXJ, int CPS>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(const Params p, const TpParams tp) {
     constexpr int CT = CW * 32;
@@ -676,10 +693,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(con
     __shared__ int s_ok;
     int r0, nrows;
     float* part;
-    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part)) return;
+    const uint32_t epoch0 = threadIdx.x == 0 ? tp_call_epoch(tp) : 0u;  // thread 0 is a consumer
+    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part)) {
+        if (threadIdx.x == 0) tp_arrive(tp, epoch0);  // no rows, or a bounded wait gave up
+        return;
+    }
     const int t = threadIdx.x, b = blockIdx.x, rows = p.rows;
     if (t == 0) {
-        s_epoch = tp.ctr[b] + 1u;
+        s_epoch = epoch0;
         s_ok = 1;
     }
     named_barrier_sync(1, CT);
@@ -693,17 +714,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(con
     if (t < tp.world) st_release_sys(tp.flags[t] + size_t(tp.rank) * kTpMaxCtas + b, epoch);
     if (t < tp.world && !wait_flag_reached(tp.flags[tp.rank] + size_t(t) * kTpMaxCtas + b, epoch)) s_ok = 0;
     named_barrier_sync(1, CT);
-    if (!s_ok) return;
-    const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
-    for (int i = t; i < nrows; i += CT) {
-        float acc = 0.f;
-        for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + r0 + i);
-        float add = 0.f;
-        if (tp.bias) add += __half2float(tp.bias[r0 + i]);
-        if (tp.residual) add += __half2float(tp.residual[r0 + i]);
-        p.y[r0 + i] = acc + add;
+    if (s_ok) {
+        const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
+        for (int i = t; i < nrows; i += CT) {
+            float acc = 0.f;
+            for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + r0 + i);
+            float add = 0.f;
+            if (tp.bias) add += __half2float(tp.bias[r0 + i]);
+            if (tp.residual) add += __half2float(tp.residual[r0 + i]);
+            p.y[r0 + i] = acc + add;
+        }
     }
-    if (t == 0) tp.ctr[b] = epoch;
+    if (t == 0) tp_arrive(tp, epoch);
 }
 
 // ===================================================================== SBULK

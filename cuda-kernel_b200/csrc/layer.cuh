@@ -100,7 +100,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_failed;
     __shared__ int s_ok;
-    __shared__ uint32_t s_xepoch;
 
     const int G = gridDim.x, b = blockIdx.x;
     const int a0 = int((long long)b * L.inter / G), a1 = int((long long)(b + 1) * L.inter / G);
@@ -171,6 +170,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
     // Every CTA reads the launch counter before it reaches the barrier; CTA 0
     // advances it only after the barrier, so the whole grid agrees on `epoch`.
     const uint32_t epoch = L.sync[0] + 1u;
+    // Thread 0 also reads the exchange call epoch (tensor parallel) and arrives on
+    // every exit path below, so the call counter advances whatever happens here.
+    const uint32_t xe = (TP && t == 0) ? tp_call_epoch(tp) : 0u;
+    auto leave = [&]() {
+        if constexpr (TP) {
+            if (t == 0) tp_arrive(tp, xe);
+        }
+    };
     float xr[kLayerMaxJ][8];
     int s = 0;
     uint32_t ph = 0;
@@ -209,7 +216,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         }
     }
     named_barrier_sync(1, CT);
-    if (s_failed) return;
+    if (s_failed) return leave();
     for (int i = t; i < nA; i += CT) {
         float ga = 0.f, ub = 0.f;
         for (int j = 0; j < CW; ++j) {
@@ -241,8 +248,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         __threadfence();
     }
     named_barrier_sync(1, CT);
-    if (!s_ok) return;
+    // advanced even when the wait gave up: the next call must not meet this call's slots
     if (b == 0 && t == 0) L.sync[0] = epoch;
+    if (!s_ok) return leave();
 
     // ---- phase 2: down rows [d0, d1) against h
     load_slice<CT>(L.h, L.inter, t, true, xr);
@@ -270,7 +278,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         }
     }
     named_barrier_sync(1, CT);
-    if (s_failed) return;
+    if (s_failed) return leave();
 
     if constexpr (!TP) {
         for (int i = t; i < nD; i += CT) {
@@ -282,10 +290,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         }
     } else {
         // The exchange of rbulk_allreduce_kernel: partial rows to every rank, flag, wait, rank-ordered sum.
-        if (t == 0) s_xepoch = tp.ctr[b] + 1u;
+        __shared__ uint32_t s_xe;
+        if (t == 0) s_xe = xe;
         named_barrier_sync(1, CT);
-        const uint32_t xe = s_xepoch;
-        const size_t par = xe & 1u;
+        const uint32_t e = s_xe;
+        const size_t par = e & 1u;
         const int rows = L.hidden;
         for (int i = t; i < nD; i += CT) {
             float a = 0.f;
@@ -293,20 +302,21 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
             for (int q = 0; q < tp.world; ++q) tp.recv[q][(par * tp.world + tp.rank) * rows + d0 + i] = a;
         }
         named_barrier_sync(1, CT);
-        if (t < tp.world) st_release_sys(tp.flags[t] + size_t(tp.rank) * kTpMaxCtas + b, xe);
-        if (t < tp.world && !wait_flag_reached(tp.flags[tp.rank] + size_t(t) * kTpMaxCtas + b, xe)) s_ok = 0;
+        if (t < tp.world) st_release_sys(tp.flags[t] + size_t(tp.rank) * kTpMaxCtas + b, e);
+        if (t < tp.world && !wait_flag_reached(tp.flags[tp.rank] + size_t(t) * kTpMaxCtas + b, e)) s_ok = 0;
         named_barrier_sync(1, CT);
-        if (!s_ok) return;
-        const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
-        for (int i = t; i < nD; i += CT) {
-            float acc = 0.f;
-            for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + d0 + i);
-            float add = 0.f;
-            if (tp.bias) add += __half2float(tp.bias[d0 + i]);
-            if (tp.residual) add += __half2float(tp.residual[d0 + i]);
-            L.y[d0 + i] = acc + add;
+        if (s_ok) {
+            const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
+            for (int i = t; i < nD; i += CT) {
+                float acc = 0.f;
+                for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + d0 + i);
+                float add = 0.f;
+                if (tp.bias) add += __half2float(tp.bias[d0 + i]);
+                if (tp.residual) add += __half2float(tp.residual[d0 + i]);
+                L.y[d0 + i] = acc + add;
+            }
         }
-        if (t == 0) tp.ctr[b] = xe;
+        leave();
     }
 }
 

@@ -2,8 +2,11 @@
 
 Each rank runs swb_ffn_tp on its shard (rows of Wg/Wu, columns of Wd), the fp32
 partial y is summed with an NCCL all-reduce, and bias + residual are applied once
-(swb_residual_epilogue). Every rank's y is compared with the unsharded CPU oracle
-at the parity tests' tolerance. Needs at least 2 GPUs; skipped otherwise.
+(swb_residual_epilogue); then the fused paths (swb_ffn_tp_fused: the down kernel
+or the whole-layer kernel sums the partials over NVLink peer memory), including
+calls of different geometries issued back to back. Every rank's y is compared
+with the unsharded CPU oracle at the parity tests' tolerance, and the ranks' y
+must be bit-identical. Needs at least 2 GPUs; skipped otherwise.
 """
 import os
 import socket
@@ -69,6 +72,13 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
         T.ffn_tp_fused(ex, x, s, bd, h, y, gate, down)  # 200+: the rank's whole layer in one kernel
         torch.cuda.synchronize()
         out.append(y.cpu().numpy().copy())
+    # geometries switched back to back with no host synchronisation: every call keeps its own y
+    seq = [(69, 80), (200, 0), (69, 87), (201, 0), (69, 83), (69, 80)] * 3
+    ys = [torch.empty_like(y) for _ in seq]
+    for (gate, down), yk in zip(seq, ys):
+        T.ffn_tp_fused(ex, x, s, bd, h, yk, gate, down)
+    torch.cuda.synchronize()
+    out.extend(yk.cpu().numpy().copy() for yk in ys)
     dist.barrier()
     assert binding.device_error() == 0
     ex.close()
