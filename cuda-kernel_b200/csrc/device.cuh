@@ -169,32 +169,36 @@ constexpr uint64_t kPeerWaitLimitNs = 1000000000ull;
 
 // Release store at system scope: every store this CTA made before the preceding
 // barrier is visible to whoever acquires this flag, on any GPU.
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// One exchange slot: an fp32 value and the call epoch that wrote it, stored as one
+// aligned 64-bit word. An aligned scalar 64-bit access is single-copy atomic, so a
+// reader that sees the epoch also sees the value: no fence or separate flag is
+// needed, on this GPU or across NVLink.
+__device__ __forceinline__ void st_slot_sys(unsigned long long* p, float v, uint32_t epoch) {
+    const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ unsigned long long ld_slot_sys(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 
-__device__ __forceinline__ float ld_volatile_f32(const float* p) {
-    float v;
-    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Waits until *f has reached `epoch` (a writer may already be one call ahead).
-__device__ __forceinline__ bool wait_flag_reached(const uint32_t* f, uint32_t epoch) {
-    if (int32_t(ld_acquire_sys(f) - epoch) >= 0) return true;
-    const uint64_t t0 = global_timer_ns();
-    while (int32_t(ld_acquire_sys(f) - epoch) < 0) {
-        if (global_timer_ns() - t0 > kPeerWaitLimitNs) {
-            atomicOr(&g_device_error, 2);
-            return false;
-        }
+// Waits (bounded) until the slot holds the value written in `epoch`. On time-out it
+// records SWB_DEVERR_PEER_TIMEOUT and returns false.
+__device__ __forceinline__ bool wait_slot(const unsigned long long* p, uint32_t epoch, float& v) {
+    unsigned long long w = ld_slot_sys(p);
+    if (uint32_t(w >> 32) != epoch) {
+        const uint64_t t0 = global_timer_ns();
+        do {
+            if (global_timer_ns() - t0 > kPeerWaitLimitNs) {
+                atomicOr(&g_device_error, 2);
+                return false;
+            }
+            w = ld_slot_sys(p);
+        } while (uint32_t(w >> 32) != epoch);
     }
+    v = __uint_as_float(uint32_t(w));
     return true;
 }
 

@@ -641,16 +641,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
 // ============================================ RBULK + one-shot all-reduce
 
 // Tensor-parallel exchange of one layer call. Rank q's exchange buffer holds
-// recv[2][world][rows] fp32 (parity-double-buffered partials from every rank),
-// flags[world][kTpMaxCtas] (flags[src][cta] = the call epoch at which src's CTA
-// published) and this rank's call counter: ctr[0] = epoch of the last finished
-// exchange call, ctr[1] = CTAs of the running call that have finished.
+// recv[2][world][rows] slots (parity-double-buffered partials from every rank;
+// a slot is one 64-bit word {fp32 value, call epoch}, see st_slot_sys) and this
+// rank's call counter: ctr[0] = epoch of the last finished exchange call,
+// ctr[1] = CTAs of the running call that have finished.
 constexpr int kTpMaxRanks = 8;
 constexpr int kTpMaxCtas = 1024;
 
 struct TpParams {
-    float* recv[kTpMaxRanks];
-    uint32_t* flags[kTpMaxRanks];
+    unsigned long long* recv[kTpMaxRanks];
     uint32_t* ctr;
     const __half* bias;      // added once after the sum (may be null)
     const __half* residual;  // added once after the sum (may be null)
@@ -664,33 +663,61 @@ struct TpParams {
 // one -- sees the new value. A per-CTA counter would not do: when consecutive
 // calls map rows to CTAs differently, a peer's CTA b could write this call's rows
 // into the parity buffer that another CTA here still reads for the previous call.
+// Epoch 0 is skipped (a never-written slot reads as epoch 0); the parity still
+// alternates across the wrap (2^32 - 1 is odd, 2 is even).
 __device__ __forceinline__ uint32_t tp_call_epoch(const TpParams& tp) {
-    return *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u;
+    const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u;
+    return e ? e : 2u;
 }
 
 __device__ __forceinline__ void tp_arrive(const TpParams& tp, uint32_t epoch) {
-    __threadfence();
     if (atomicInc(tp.ctr + 1, gridDim.x - 1u) == gridDim.x - 1u)
         *reinterpret_cast<volatile uint32_t*>(tp.ctr) = epoch;
 }
 
+// Rows [r0, r0 + n) of y: this rank's partial `own(i)` goes to slot
+// [parity][my rank][row] of every other rank; then each row sums every rank's
+// partial in rank order -- the same order on every rank, so y is bit-identical
+// everywhere -- plus bias and residual. A rank can run at most one call ahead of
+// a peer (each call waits for that peer's slots), so the parity double buffer
+// keeps a slot from being rewritten before it is read.
+template <int CT, class Own>
+__device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, float* y,
+                                                 Own own) {
+    const int t = threadIdx.x;
+    const size_t par = epoch & 1u;
+    for (int i = t; i < n; i += CT) {
+        const float a = own(i);
+        for (int q = 0; q < tp.world; ++q)
+            if (q != tp.rank) st_slot_sys(tp.recv[q] + (par * tp.world + tp.rank) * rows + r0 + i, a, epoch);
+    }
+    const unsigned long long* mine = tp.recv[tp.rank] + par * tp.world * rows;
+    bool ok = true;
+    for (int i = t; i < n; i += CT) {
+        float acc = 0.f;
+        for (int q = 0; q < tp.world; ++q) {
+            float v = 0.f;
+            if (q == tp.rank) v = own(i);
+            else if (ok) ok = wait_slot(mine + size_t(q) * rows + r0 + i, epoch, v);
+            acc += v;
+        }
+        if (!ok) break;  // a peer did not deliver: the error word is set, y is not written
+        float add = 0.f;
+        if (tp.bias) add += __half2float(tp.bias[r0 + i]);
+        if (tp.residual) add += __half2float(tp.residual[r0 + i]);
+        y[r0 + i] = acc + add;
+    }
+}
+
 // The down projection of a tensor-parallel rank with the all-reduce fused into
-// its epilogue. Every rank runs the same grid and row partition, so CTA b owns
-// rows [r0, r1) of y on every rank. CTA b: (1) stores its partial rows into
-// slot [parity][my rank] of every rank's receive buffer (NVLink peer stores);
-// (2) publishes flags[my rank][b] = epoch on every rank with a system-scope
-// release; (3) waits (bounded) until every rank's CTA b has published epoch;
-// (4) sums the ranks' partials in rank order -- the same order on every rank, so
-// y is bit-identical everywhere -- adds bias + residual and writes y. The epoch
-// lives in device memory (tp_call_epoch), so graph replays need no reset; a rank
-// can run at most one call ahead of a peer (it waits on that peer every call),
-// which the parity double buffer and the "reached" flag test cover.
+// its epilogue (tp_exchange_rows). Every rank runs the same grid and row
+// partition, so CTA b owns rows [r0, r1) of y on every rank. The epoch lives in
+// device memory (tp_call_epoch), so graph replays need no reset.
 template <int CW, int MAXJ, int CPS>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(const Params p, const TpParams tp) {
     constexpr int CT = CW * 32;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint32_t s_epoch;
-    __shared__ int s_ok;
     int r0, nrows;
     float* part;
     const uint32_t epoch0 = threadIdx.x == 0 ? tp_call_epoch(tp) : 0u;  // thread 0 is a consumer
@@ -698,34 +725,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(con
         if (threadIdx.x == 0) tp_arrive(tp, epoch0);  // no rows, or a bounded wait gave up
         return;
     }
-    const int t = threadIdx.x, b = blockIdx.x, rows = p.rows;
-    if (t == 0) {
-        s_epoch = epoch0;
-        s_ok = 1;
-    }
+    const int t = threadIdx.x;
+    if (t == 0) s_epoch = epoch0;
     named_barrier_sync(1, CT);
-    const uint32_t epoch = s_epoch;
-    const size_t par = epoch & 1u;
-    for (int i = t; i < nrows; i += CT) {
-        const float a = row_sum<CW, 1>(part, i, 0);
-        for (int q = 0; q < tp.world; ++q) tp.recv[q][(par * tp.world + tp.rank) * rows + r0 + i] = a;
-    }
-    named_barrier_sync(1, CT);
-    if (t < tp.world) st_release_sys(tp.flags[t] + size_t(tp.rank) * kTpMaxCtas + b, epoch);
-    if (t < tp.world && !wait_flag_reached(tp.flags[tp.rank] + size_t(t) * kTpMaxCtas + b, epoch)) s_ok = 0;
-    named_barrier_sync(1, CT);
-    if (s_ok) {
-        const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
-        for (int i = t; i < nrows; i += CT) {
-            float acc = 0.f;
-            for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + r0 + i);
-            float add = 0.f;
-            if (tp.bias) add += __half2float(tp.bias[r0 + i]);
-            if (tp.residual) add += __half2float(tp.residual[r0 + i]);
-            p.y[r0 + i] = acc + add;
-        }
-    }
-    if (t == 0) tp_arrive(tp, epoch);
+    tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.y, [&](int i) { return row_sum<CW, 1>(part, i, 0); });
+    if (t == 0) tp_arrive(tp, s_epoch);
 }
 
 // ===================================================================== SBULK

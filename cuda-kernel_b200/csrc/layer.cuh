@@ -289,33 +289,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
             L.y[d0 + i] = a;
         }
     } else {
-        // The exchange of rbulk_allreduce_kernel: partial rows to every rank, flag, wait, rank-ordered sum.
+        // The exchange of rbulk_allreduce_kernel: partial rows to every rank, rank-ordered sum.
         __shared__ uint32_t s_xe;
         if (t == 0) s_xe = xe;
         named_barrier_sync(1, CT);
-        const uint32_t e = s_xe;
-        const size_t par = e & 1u;
-        const int rows = L.hidden;
-        for (int i = t; i < nD; i += CT) {
+        tp_exchange_rows<CT>(tp, s_xe, L.hidden, d0, nD, L.y, [&](int i) {
             float a = 0.f;
             for (int j = 0; j < CW; ++j) a += part2[size_t(i) * CW + j];
-            for (int q = 0; q < tp.world; ++q) tp.recv[q][(par * tp.world + tp.rank) * rows + d0 + i] = a;
-        }
-        named_barrier_sync(1, CT);
-        if (t < tp.world) st_release_sys(tp.flags[t] + size_t(tp.rank) * kTpMaxCtas + b, e);
-        if (t < tp.world && !wait_flag_reached(tp.flags[tp.rank] + size_t(t) * kTpMaxCtas + b, e)) s_ok = 0;
-        named_barrier_sync(1, CT);
-        if (s_ok) {
-            const float* mine = tp.recv[tp.rank] + par * tp.world * rows;
-            for (int i = t; i < nD; i += CT) {
-                float acc = 0.f;
-                for (int q = 0; q < tp.world; ++q) acc += ld_volatile_f32(mine + size_t(q) * rows + d0 + i);
-                float add = 0.f;
-                if (tp.bias) add += __half2float(tp.bias[d0 + i]);
-                if (tp.residual) add += __half2float(tp.residual[d0 + i]);
-                L.y[d0 + i] = acc + add;
-            }
-        }
+            return a;
+        });
         leave();
     }
 }

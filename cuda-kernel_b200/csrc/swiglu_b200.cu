@@ -239,7 +239,7 @@ int launch_rbulk_ar(Params p, const TpParams& tp, cudaStream_t stream, bool pdl)
     const int sms = sm_count();
     if (sms <= 0) return check_launch();
     const int G = std::min(sms * CPS, p.rows);
-    if (G > kTpMaxCtas) return fail(SWB_E_UNSUPPORTED, "grid larger than the exchange flag table");
+    if (G > kTpMaxCtas) return fail(SWB_E_UNSUPPORTED, "grid larger than the exchange supports");
     const int rows_per_cta = (p.rows + G - 1) / G;
     const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
     const size_t row_bytes = size_t(p.cols) * 2;
@@ -719,17 +719,31 @@ extern "C" int swb_ffn_noalloc(int gate_config, int down_config, const void* wg,
 
 // ---------------------------------------------------------------------------
 // Tensor-parallel exchange: one per rank, allocated once at set-up.
+// A rank's exchange buffer (one cudaMalloc, mapped by every peer through CUDA IPC):
+//   [recv slots: 2 parities x world x rows x 8 B][call counter: 256 B][layer grid-barrier slots]
 struct swb_tp {
     int rank, world, rows, device;
     void* local;
-    size_t bytes, recv_bytes, flag_bytes;
+    size_t bytes, recv_bytes;
     void* peer[kTpMaxRanks];
     bool connected;
 };
 
 namespace {
-size_t tp_recv_bytes(int world, int rows) { return align_up(size_t(2) * world * rows * 4, 256); }
-size_t tp_flag_bytes(int world) { return align_up(size_t(world) * kTpMaxCtas * 4, 256); }
+constexpr size_t kTpCounterBytes = 256;
+size_t tp_recv_bytes(int world, int rows) { return align_up(size_t(2) * world * rows * 8, 256); }
+
+TpParams tp_params(const swb_tp* tp, const void* bd, const void* x) {
+    TpParams t;
+    std::memset(&t, 0, sizeof t);
+    for (int q = 0; q < tp->world; ++q) t.recv[q] = static_cast<unsigned long long*>(tp->peer[q]);
+    t.ctr = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes);
+    t.bias = static_cast<const __half*>(bd);
+    t.residual = static_cast<const __half*>(x);
+    t.rank = tp->rank;
+    t.world = tp->world;
+    return t;
+}
 }  // namespace
 
 extern "C" {
@@ -743,8 +757,7 @@ int swb_tp_create(int rank, int world, int rows, swb_tp_t** out) {
     tp->world = world;
     tp->rows = rows;
     tp->recv_bytes = tp_recv_bytes(world, rows);
-    tp->flag_bytes = tp_flag_bytes(world);
-    tp->bytes = tp->recv_bytes + tp->flag_bytes + align_up(size_t(kTpMaxCtas) * 4, 256) + SWB_LAYER_WORKSPACE_BYTES;
+    tp->bytes = tp->recv_bytes + kTpCounterBytes + SWB_LAYER_WORKSPACE_BYTES;
     cudaError_t e = cudaGetDevice(&tp->device);
     if (e == cudaSuccess) e = cudaMalloc(&tp->local, tp->bytes);  // set-up time, once per rank
     if (e == cudaSuccess) e = cudaMemset(tp->local, 0, tp->bytes);
@@ -819,22 +832,8 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
         L.y = y;
         L.hidden = hidden;
         L.inter = shard;
-        char* base = static_cast<char*>(tp->local);
-        L.sync = reinterpret_cast<uint32_t*>(base + tp->recv_bytes + tp->flag_bytes +
-                                             align_up(size_t(kTpMaxCtas) * 4, 256));
-        TpParams t;
-        std::memset(&t, 0, sizeof t);
-        for (int q = 0; q < tp->world; ++q) {
-            char* pb = static_cast<char*>(tp->peer[q]);
-            t.recv[q] = reinterpret_cast<float*>(pb);
-            t.flags[q] = reinterpret_cast<uint32_t*>(pb + tp->recv_bytes);
-        }
-        t.ctr = reinterpret_cast<uint32_t*>(base + tp->recv_bytes + tp->flag_bytes);
-        t.bias = static_cast<const __half*>(bd);
-        t.residual = static_cast<const __half*>(x);
-        t.rank = tp->rank;
-        t.world = tp->world;
-        return dispatch_layer<true>(gate_config, L, t, static_cast<cudaStream_t>(stream));
+        L.sync = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + kTpCounterBytes);
+        return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream));
     }
     if (int rc = swb_gate(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream))
         return rc;
@@ -844,19 +843,7 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
     p.y = y;
     p.rows = hidden;
     p.cols = shard;
-    TpParams t;
-    std::memset(&t, 0, sizeof t);
-    for (int q = 0; q < tp->world; ++q) {
-        char* base = static_cast<char*>(tp->peer[q]);
-        t.recv[q] = reinterpret_cast<float*>(base);
-        t.flags[q] = reinterpret_cast<uint32_t*>(base + tp->recv_bytes);
-    }
-    t.ctr = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + tp->flag_bytes);
-    t.bias = static_cast<const __half*>(bd);
-    t.residual = static_cast<const __half*>(x);
-    t.rank = tp->rank;
-    t.world = tp->world;
-    return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true);
+    return dispatch_allreduce(down_config, p, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream), true);
 }
 
 }  // extern "C"

@@ -6,8 +6,10 @@ it allocates it (C ABI ``swb_tp_create``), shares its CUDA IPC handle with every
 rank through ``torch.distributed`` and maps the peers' buffers
 (``swb_tp_connect``). ``ffn_tp_fused`` then runs a rank's layer as two kernels:
 the gate on the shard, and the down projection whose epilogue stores its partial
-rows into every rank's buffer over NVLink, waits for the peers' flags and writes
-y = sum of partials + bias + residual (identical on every rank). ``shard`` cuts
+rows into every rank's buffer over NVLink (each value with the call's epoch in one
+64-bit word), waits until the peers' words carry the epoch and writes
+y = sum of partials + bias + residual (identical on every rank); or, with a
+fused-layer id, the whole rank's layer in one kernel. ``shard`` cuts
 the weights for a rank. The NCCL alternative (``swb_ffn_tp`` + all-reduce +
 ``swb_residual_epilogue``) stays available as the baseline.
 """

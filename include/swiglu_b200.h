@@ -153,10 +153,11 @@ SWB_API int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, c
 
 /* Fused tensor parallel (no counterpart in the reference). The down projection of
  * each rank sums the ranks' partial y itself: its CTAs store their partial rows
- * straight into every peer's exchange buffer over NVLink, publish a flag with a
- * system-scope release, wait (bounded: SWB_DEVERR_PEER_TIMEOUT, then no output)
- * for the same CTA of every rank, and add the partials in rank order plus bias
- * and residual -- no NCCL call and no separate epilogue kernel. Set-up, once per
+ * straight into every peer's exchange buffer over NVLink, each value together
+ * with the call's epoch in one 64-bit word (no fence, no separate flag), wait
+ * (bounded: SWB_DEVERR_PEER_TIMEOUT, then no output) until every rank's words of
+ * their rows carry the epoch, and add the partials in rank order plus bias and
+ * residual -- no NCCL call and no separate epilogue kernel. Set-up, once per
  * rank: swb_tp_create (allocates this rank's exchange buffer), share
  * swb_tp_ipc_handle with every rank (any transport), swb_tp_connect with all
  * handles in rank order. Every rank must then make the same sequence of
