@@ -46,7 +46,25 @@ struct Params {
     int rows_per_block;  // sbulk_kernel: rows per CTA index (unit of work stealing)
     int blocks;          // sbulk_kernel: number of row blocks (= grid size)
     int block_stride;    // sbulk_kernel: A in row_block = (cta * A) mod blocks, gcd(A, blocks) = 1
+    // Tensor-parallel exchange call epoch (null otherwise): the gate kernel of a
+    // call advances it (advance_call_epoch); the fused down kernel reads it after
+    // griddepcontrol.wait, so both kernels of the call agree on it.
+    uint32_t* epoch;
 };
+
+// Epochs run 1, 2, ..., 2^32 - 1, 2, 3, ...: 0 is skipped (a never-written exchange
+// slot reads as epoch 0) and the parity still alternates across the wrap.
+__host__ __device__ __forceinline__ uint32_t next_epoch(uint32_t e) { return e + 1u ? e + 1u : 2u; }
+
+// First thing in every kernel that can run as the gate of a tensor-parallel call.
+// The previous call's down kernel has completed (the gate is launched in stream
+// order), so this single writer cannot race its read.
+__device__ __forceinline__ void advance_call_epoch(const Params& p) {
+    if (p.epoch && blockIdx.x == 0 && threadIdx.x == 0) {
+        volatile uint32_t* e = p.epoch;
+        *e = next_epoch(*e);
+    }
+}
 
 template <int MODE>
 __device__ __forceinline__ void write_row(const Params& p, int row, float a, float b) {
@@ -168,6 +186,7 @@ __device__ __forceinline__ void stage_x(const __half* __restrict__ x, float* xs,
 
 template <int WPR, int ROWS, int PACK, int UNROLL, int MODE>
 __global__ void __launch_bounds__(32 * WPR * ROWS) ldg_kernel(const Params p) {
+    advance_call_epoch(p);
     static_assert(WPR > 0 && (WPR & (WPR - 1)) == 0 && ROWS > 0 && 32 * WPR * ROWS <= 1024, "geometry");
     static_assert(PACK == 2 || PACK == 8, "pack");
     constexpr bool GATED = MODE == MODE_GATE;
@@ -319,6 +338,7 @@ __host__ __device__ inline BulkLayout bulk_layout(int nm, int chunk, int stages,
 
 template <int CW, int CHUNK, int MODE>
 __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) {
+    advance_call_epoch(p);
     static_assert(CHUNK % 8 == 0 && CHUNK > 0, "chunk must be whole 16-byte vectors");
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
@@ -479,7 +499,7 @@ __host__ __device__ inline BulkLayout rbulk_layout(int nm, int row_stage, int co
 // Returns false on the producer warp and when a bounded wait gave up.
 template <int CW, int MAXJ, int MODE>
 __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* smem, int& r0_out, int& nrows_out,
-                                             float*& part_out) {
+                                             float*& part_out, uint32_t* epoch_out = nullptr) {
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
     constexpr int CT = CW * 32;
@@ -550,6 +570,8 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
+    // the call epoch the gate kernel advanced (fused tensor-parallel down only)
+    if (epoch_out && t == 0) *epoch_out = *reinterpret_cast<volatile const uint32_t*>(p.epoch);
     float xr[MAXJ][8];
     const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
 #pragma unroll
@@ -628,6 +650,7 @@ __device__ __forceinline__ float row_sum(const float* part, int i, int m) {
 
 template <int CW, int MAXJ, int CPS, int MODE>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params p) {
+    advance_call_epoch(p);
     constexpr int NM = MODE == MODE_GATE ? 2 : 1;
     constexpr int CT = CW * 32;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -643,8 +666,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
 // Tensor-parallel exchange of one layer call. Rank q's exchange buffer holds
 // recv[2][world][rows] slots (parity-double-buffered partials from every rank;
 // a slot is one 64-bit word {fp32 value, call epoch}, see st_slot_sys) and this
-// rank's call counter: ctr[0] = epoch of the last finished exchange call,
-// ctr[1] = CTAs of the running call that have finished.
+// rank's call epoch ctr[0]. Each call advances the epoch exactly once: the gate
+// kernel does it (Params::epoch) before the fused down kernel reads it, or the
+// fused layer kernel's CTA 0 stores the epoch every CTA read before the grid
+// barrier. One epoch per call, the same for every CTA whatever the grid: with a
+// per-CTA counter, consecutive calls that map rows to CTAs differently could let
+// a peer's CTA b write this call's rows into the parity buffer that another CTA
+// here still reads for the previous call. After a device error the exchange must
+// be recreated (the epochs of the ranks may no longer agree).
 constexpr int kTpMaxRanks = 8;
 constexpr int kTpMaxCtas = 1024;
 
@@ -656,24 +685,6 @@ struct TpParams {
     int rank;
     int world;
 };
-
-// One epoch per exchange call, the same for every CTA whatever the grid: each CTA
-// reads it before it arrives, and the last CTA to arrive (on every exit path,
-// failures included) advances it, so the next call -- stream-ordered after this
-// one -- sees the new value. A per-CTA counter would not do: when consecutive
-// calls map rows to CTAs differently, a peer's CTA b could write this call's rows
-// into the parity buffer that another CTA here still reads for the previous call.
-// Epoch 0 is skipped (a never-written slot reads as epoch 0); the parity still
-// alternates across the wrap (2^32 - 1 is odd, 2 is even).
-__device__ __forceinline__ uint32_t tp_call_epoch(const TpParams& tp) {
-    const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u;
-    return e ? e : 2u;
-}
-
-__device__ __forceinline__ void tp_arrive(const TpParams& tp, uint32_t epoch) {
-    if (atomicInc(tp.ctr + 1, gridDim.x - 1u) == gridDim.x - 1u)
-        *reinterpret_cast<volatile uint32_t*>(tp.ctr) = epoch;
-}
 
 // Rows [r0, r0 + n) of y: this rank's partial `own(i)` goes to slot
 // [parity][my rank][row] of every other rank; then each row sums every rank's
@@ -712,7 +723,7 @@ __device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t ep
 // The down projection of a tensor-parallel rank with the all-reduce fused into
 // its epilogue (tp_exchange_rows). Every rank runs the same grid and row
 // partition, so CTA b owns rows [r0, r1) of y on every rank. The epoch lives in
-// device memory (tp_call_epoch), so graph replays need no reset.
+// device memory (advanced by the gate kernel), so graph replays need no reset.
 template <int CW, int MAXJ, int CPS>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(const Params p, const TpParams tp) {
     constexpr int CT = CW * 32;
@@ -720,16 +731,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(con
     __shared__ uint32_t s_epoch;
     int r0, nrows;
     float* part;
-    const uint32_t epoch0 = threadIdx.x == 0 ? tp_call_epoch(tp) : 0u;  // thread 0 is a consumer
-    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part)) {
-        if (threadIdx.x == 0) tp_arrive(tp, epoch0);  // no rows, or a bounded wait gave up
-        return;
-    }
-    const int t = threadIdx.x;
-    if (t == 0) s_epoch = epoch0;
+    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part, &s_epoch)) return;
     named_barrier_sync(1, CT);
     tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.y, [&](int i) { return row_sum<CW, 1>(part, i, 0); });
-    if (t == 0) tp_arrive(tp, s_epoch);
 }
 
 // ===================================================================== SBULK
@@ -763,6 +767,7 @@ __host__ __device__ inline StealLayout sbulk_layout(int nm, int row_stage, int c
 // deterministic whatever the stealing order.
 template <int CW, int MAXJ, int CPS, int MODE>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params p) {
+    advance_call_epoch(p);
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
     constexpr int CT = CW * 32;

@@ -28,7 +28,7 @@ struct LayerParams {
     const __half* bd;
     __half* h;
     float* y;
-    uint32_t* sync;  // [0]: launch counter; [1 + b]: epoch at which CTA b reached the barrier
+    uint32_t* sync;  // [0]: grid-barrier word (zero before the first call; see layer_kernel)
     int hidden;      // phase 1: inter rows x hidden cols; phase 2: hidden rows x inter cols
     int inter;
     int rs1, rs2;    // whole rows per ring stage in each phase
@@ -49,10 +49,6 @@ __host__ __device__ inline LayerLayout layer_layout(int stage_bytes, int stages,
     L.part2 = align_up(L.part1 + size_t(rpc1) * cw * 2 * 4, 16);
     L.total = align_up(L.part2 + size_t(rpc2) * cw * 4, 16);
     return L;
-}
-
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
@@ -167,17 +163,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output
-    // Every CTA reads the launch counter before it reaches the barrier; CTA 0
-    // advances it only after the barrier, so the whole grid agrees on `epoch`.
-    const uint32_t epoch = L.sync[0] + 1u;
-    // Thread 0 also reads the exchange call epoch (tensor parallel) and arrives on
-    // every exit path below, so the call counter advances whatever happens here.
-    const uint32_t xe = (TP && t == 0) ? tp_call_epoch(tp) : 0u;
-    auto leave = [&]() {
-        if constexpr (TP) {
-            if (t == 0) tp_arrive(tp, xe);
-        }
-    };
+    // Tensor parallel: every CTA reads this call's exchange epoch before it reaches
+    // the grid barrier; CTA 0 stores it after the barrier.
+    const uint32_t xe = (TP && t == 0) ? next_epoch(*reinterpret_cast<volatile const uint32_t*>(tp.ctr)) : 0u;
     float xr[kLayerMaxJ][8];
     int s = 0;
     uint32_t ph = 0;
@@ -216,7 +204,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         }
     }
     named_barrier_sync(1, CT);
-    if (s_failed) return leave();
+    if (s_failed) return;
     for (int i = t; i < nA; i += CT) {
         float ga = 0.f, ub = 0.f;
         for (int j = 0; j < CW; ++j) {
@@ -228,29 +216,30 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         L.h[a0 + i] = __float2half_rn(silu(ga) * ub);
     }
 
-    // ---- grid barrier: all of h written and visible (bounded wait)
+    // ---- grid barrier: all of h written and visible (bounded wait). One word:
+    // CTA 0 adds 2^31 - (G - 1), every other CTA adds 1, so the adds of one
+    // barrier sum to 2^31 and the word's top bit flips exactly when the last CTA
+    // arrives (its low 31 bits stay zero between barriers, whatever the grid).
+    // Each CTA waits for the top bit to differ from the one it saw on arrival: a
+    // single L2 round trip per poll, instead of one per CTA of the grid.
     named_barrier_sync(1, CT);
     if (t == 0) {
-        __threadfence();
-        st_release_gpu(L.sync + 1 + b, epoch);
-    }
-    if (warp == 0) {
+        __threadfence();  // this CTA's h (ordered before by the CTA barrier) visible at gpu scope
+        const uint32_t add = b == 0 ? 0x80000000u - uint32_t(G - 1) : 1u;
+        const uint32_t seen = atomicAdd(L.sync, add) & 0x80000000u;
         const uint64_t t0 = global_timer_ns();
-        for (int j = lane; j < G; j += 32) {
-            while (int32_t(ld_acquire_gpu(L.sync + 1 + j) - epoch) < 0) {
-                if (global_timer_ns() - t0 > kWaitLimitNs) {
-                    atomicOr(&g_device_error, 1);
-                    s_ok = 0;
-                    break;
-                }
+        while ((ld_acquire_gpu(L.sync) & 0x80000000u) == seen) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&g_device_error, 1);
+                s_ok = 0;
+                break;
             }
         }
         __threadfence();
     }
+    if (TP && b == 0 && t == 0) *reinterpret_cast<volatile uint32_t*>(tp.ctr) = xe;
     named_barrier_sync(1, CT);
-    // advanced even when the wait gave up: the next call must not meet this call's slots
-    if (b == 0 && t == 0) L.sync[0] = epoch;
-    if (!s_ok) return leave();
+    if (!s_ok) return;
 
     // ---- phase 2: down rows [d0, d1) against h
     load_slice<CT>(L.h, L.inter, t, true, xr);
@@ -278,7 +267,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         }
     }
     named_barrier_sync(1, CT);
-    if (s_failed) return leave();
+    if (s_failed) return;
 
     if constexpr (!TP) {
         for (int i = t; i < nD; i += CT) {
@@ -298,7 +287,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
             for (int j = 0; j < CW; ++j) a += part2[size_t(i) * CW + j];
             return a;
         });
-        leave();
     }
 }
 

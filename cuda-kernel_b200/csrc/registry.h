@@ -95,4 +95,9 @@
     X(201, 4, 2, 32768, 4)      \
     X(202, 8, 2, 16384, 8)      \
     X(204, 4, 2, 16384, 8)      \
-    X(205, 8, 1, 16384, 12)
+    X(205, 8, 1, 16384, 12)     \
+    X(206, 8, 1, 65536, 3)      \
+    X(207, 16, 1, 65536, 3)     \
+    X(208, 8, 1, 49152, 4)      \
+    X(209, 8, 2, 49152, 2)      \
+    X(210, 16, 1, 49152, 4)

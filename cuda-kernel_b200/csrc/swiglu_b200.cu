@@ -552,12 +552,18 @@ int swb_config_info(int64_t id, swb_config_t* out) {
     return SWB_OK;
 }
 
-int swb_gate(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu, void* h,
-             int rows, int cols, int model_round, void* stream) {
+}  // extern "C"
+
+namespace {
+// swb_gate; `epoch` (tensor parallel) is the exchange's call epoch, which the
+// kernel advances for the fused down kernel that follows.
+int gate_impl(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu, void* h,
+              int rows, int cols, int model_round, void* stream, uint32_t* epoch) {
     if (rows <= 0 || cols <= 0 || !wg || !x) return fail(SWB_E_INPUT);
     if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
     if (!find_config(config)) return fail(SWB_E_CONFIG);
     Params p = make_params();
+    p.epoch = epoch;
     p.w = static_cast<const __half*>(wg);
     p.u = static_cast<const __half*>(wu);
     p.x = static_cast<const __half*>(x);
@@ -568,6 +574,14 @@ int swb_gate(int config, const void* wg, const void* wu, const void* x, const vo
     p.cols = cols;
     p.model_round = model_round ? 1 : 0;
     return dispatch<MODE_GATE>(config, p, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+extern "C" {
+
+int swb_gate(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu, void* h,
+             int rows, int cols, int model_round, void* stream) {
+    return gate_impl(config, wg, wu, x, bg, bu, h, rows, cols, model_round, stream, nullptr);
 }
 
 namespace {
@@ -835,7 +849,10 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
         L.sync = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + kTpCounterBytes);
         return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream));
     }
-    if (int rc = swb_gate(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream))
+    const TpParams t = tp_params(tp, bd, x);
+    // the gate kernel advances the call epoch; the down kernel reads it after griddepcontrol.wait
+    if (int rc = gate_impl(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream,
+                           t.ctr))
         return rc;
     Params p = make_params();
     p.w = static_cast<const __half*>(wd_shard);
@@ -843,7 +860,8 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
     p.y = y;
     p.rows = hidden;
     p.cols = shard;
-    return dispatch_allreduce(down_config, p, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream), true);
+    p.epoch = t.ctr;
+    return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true);
 }
 
 }  // extern "C"
