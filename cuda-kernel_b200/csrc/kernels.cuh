@@ -52,18 +52,16 @@ struct Params {
     uint32_t* epoch;
 };
 
-// Epochs run 1, 2, ..., 2^32 - 1, 2, 3, ...: 0 is skipped (a never-written exchange
-// slot reads as epoch 0) and the parity still alternates across the wrap.
-__host__ __device__ __forceinline__ uint32_t next_epoch(uint32_t e) { return e + 1u ? e + 1u : 2u; }
-
-// First thing in every kernel that can run as the gate of a tensor-parallel call.
-// The previous call's down kernel has completed (the gate is launched in stream
-// order), so this single writer cannot race its read.
+// First thing in every kernel that can run as the gate of a tensor-parallel call:
+// one fire-and-forget add (no thread waits for it). The previous call's down
+// kernel, which read the epoch, completed before this gate started (the gate is
+// launched in stream order); this call's down kernel reads it only after
+// griddepcontrol.wait, when this grid's memory operations are complete. Epochs
+// start at 1 in a zeroed exchange, so a slot's epoch field is 0 only until its
+// first write; every call writes each slot a reader of its parity waits on, so
+// when the counter wraps back to 0 no such slot still holds that value.
 __device__ __forceinline__ void advance_call_epoch(const Params& p) {
-    if (p.epoch && blockIdx.x == 0 && threadIdx.x == 0) {
-        volatile uint32_t* e = p.epoch;
-        *e = next_epoch(*e);
-    }
+    if (p.epoch && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(p.epoch, 1u);
 }
 
 template <int MODE>
@@ -487,6 +485,63 @@ __host__ __device__ inline BulkLayout rbulk_layout(int nm, int row_stage, int co
     return L;
 }
 
+// Dot products of the `ru` rows of one ring stage with the consumer's register
+// slice xr (vectors t + j*CT, j < J), RG rows at a time: the RG butterfly
+// reductions run interleaved, so rows that give each thread only a vector or two
+// are not bound by one dependent shuffle chain per row. Each row's result is the
+// same xor butterfly as warp_sum's. Lane 0 stores the warp partials of row
+// prow0 + r into part[row][warp][matrix].
+template <int CW, int MAXJ, int NM, int RG, int J>
+__device__ __forceinline__ void stage_rows(const __half* sw, int ru, int rs, int cols, int nv, const float (&xr)[MAXJ][8],
+                                           float* part, int prow0) {
+    static_assert(J <= MAXJ, "vectors per thread");
+    constexpr int CT = CW * 32;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    for (int r = 0; r < ru; r += RG) {
+        float acc[RG][NM][4];
+#pragma unroll
+        for (int g = 0; g < RG; ++g)
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[g][m][q] = 0.f;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const int v = t + j * CT;
+            if (v < nv) {
+#pragma unroll
+                for (int g = 0; g < RG; ++g) {
+                    if (r + g < ru) {
+                        const __half* wv = sw + size_t(r + g) * cols + size_t(v) * 8;
+                        dot8(*reinterpret_cast<const uint4*>(wv), xr[j], acc[g][0]);
+                        if constexpr (NM == 2)
+                            dot8(*reinterpret_cast<const uint4*>(wv + size_t(rs) * cols), xr[j], acc[g][1]);
+                    }
+                }
+            }
+        }
+        float red[RG][NM];
+#pragma unroll
+        for (int g = 0; g < RG; ++g)
+#pragma unroll
+            for (int m = 0; m < NM; ++m) red[g][m] = fold4(acc[g][m]);
+#pragma unroll
+        for (int d = 16; d; d >>= 1)
+#pragma unroll
+            for (int g = 0; g < RG; ++g)
+#pragma unroll
+                for (int m = 0; m < NM; ++m) red[g][m] += __shfl_xor_sync(0xffffffffu, red[g][m], d);
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < RG; ++g)
+                if (r + g < ru)
+#pragma unroll
+                    for (int m = 0; m < NM; ++m) part[(size_t(prow0 + r + g) * CW + warp) * NM + m] = red[g][m];
+        }
+    }
+}
+
+
 // Persistent row-stage streaming. CTA b owns rows [b*rows/G, (b+1)*rows/G).
 // A producer thread streams them with one cp.async.bulk per matrix per ring
 // stage; a stage holds `row_stage` whole rows, which are contiguous in a
@@ -596,46 +651,34 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
         }
     }
 
-    int s = 0;
-    uint32_t ph = 0;
-    for (int k = 0; k < units; ++k) {
-        if (!mbar_wait(smem_u32(full + s), ph)) {
-            s_failed = 1;
-            break;
-        }
-        const int row0 = r0 + k * rs;
-        const int ru = min(rs, r1 - row0);
-        const __half* sw = ring + size_t(s) * stage_halves;
-        for (int r = 0; r < ru; ++r) {
-            float acc[NM][4];
-#pragma unroll
-            for (int m = 0; m < NM; ++m)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
-            const __half* wrow = sw + size_t(r) * cols;
-#pragma unroll
-            for (int j = 0; j < MAXJ; ++j) {
-                const int v = t + j * CT;
-                if (v < nv) {
-                    dot8(*reinterpret_cast<const uint4*>(wrow + size_t(v) * 8), xr[j], acc[0]);
-                    if constexpr (GATED)
-                        dot8(*reinterpret_cast<const uint4*>(wrow + size_t(rs) * cols + size_t(v) * 8), xr[j],
-                             acc[1]);
-                }
+    // Rows per reduction group by the vectors each thread holds (jn): short rows
+    // reduce 8 / NM at once. The choice is made once, outside the stage loop, so
+    // each loop keeps only the part of xr it reads in registers.
+    auto consume = [&](auto rg, auto jv) {
+        constexpr int RG = decltype(rg)::value, J = decltype(jv)::value;
+        int s = 0;
+        uint32_t ph = 0;
+        for (int k = 0; k < units; ++k) {
+            if (!mbar_wait(smem_u32(full + s), ph)) {
+                s_failed = 1;
+                break;
             }
-            const float a = warp_sum(fold4(acc[0]));
-            float b = 0.f;
-            if constexpr (GATED) b = warp_sum(fold4(acc[1]));
-            if (lane == 0) {
-                const size_t slot = (size_t(row0 - r0 + r) * CW + warp) * NM;
-                part[slot] = a;
-                if constexpr (GATED) part[slot + 1] = b;
-            }
+            const int row0 = r0 + k * rs;
+            const int ru = min(rs, r1 - row0);
+            const __half* sw = ring + size_t(s) * stage_halves;
+            stage_rows<CW, MAXJ, NM, RG, J>(sw, ru, rs, cols, nv, xr, part, row0 - r0);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(empty + s));
+            if (++s == stages) { s = 0; ph ^= 1u; }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(empty + s));
-        if (++s == stages) { s = 0; ph ^= 1u; }
-    }
+    };
+    const int jn = (nv + CT - 1) / CT;
+    if (jn <= 1)
+        consume(std::integral_constant<int, 8 / NM>{}, std::integral_constant<int, 1>{});
+    else if (jn <= 2)
+        consume(std::integral_constant<int, 4 / NM>{}, std::integral_constant<int, (MAXJ < 2 ? MAXJ : 2)>{});
+    else
+        consume(std::integral_constant<int, 1>{}, std::integral_constant<int, MAXJ>{});
     named_barrier_sync(1, CT);
     return s_failed == 0;
 }
@@ -695,18 +738,27 @@ struct TpParams {
 template <int CT, class Own>
 __device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, float* y,
                                                  Own own) {
+    // rank loops run to the compile-time bound, so recv[] is indexed by constants
+    // and stays in the kernel's parameter space
     const int t = threadIdx.x;
     const size_t par = epoch & 1u;
     for (int i = t; i < n; i += CT) {
         const float a = own(i);
-        for (int q = 0; q < tp.world; ++q)
-            if (q != tp.rank) st_slot_sys(tp.recv[q] + (par * tp.world + tp.rank) * rows + r0 + i, a, epoch);
+#pragma unroll
+        for (int q = 0; q < kTpMaxRanks; ++q)
+            if (q < tp.world && q != tp.rank)
+                st_slot_sys(tp.recv[q] + (par * tp.world + tp.rank) * rows + r0 + i, a, epoch);
     }
-    const unsigned long long* mine = tp.recv[tp.rank] + par * tp.world * rows;
+    const unsigned long long* mine = tp.recv[0] + par * tp.world * rows;
+#pragma unroll
+    for (int q = 1; q < kTpMaxRanks; ++q)
+        if (q == tp.rank) mine = tp.recv[q] + par * tp.world * rows;
     bool ok = true;
     for (int i = t; i < n; i += CT) {
         float acc = 0.f;
-        for (int q = 0; q < tp.world; ++q) {
+#pragma unroll
+        for (int q = 0; q < kTpMaxRanks; ++q) {
+            if (q >= tp.world) break;
             float v = 0.f;
             if (q == tp.rank) v = own(i);
             else if (ok) ok = wait_slot(mine + size_t(q) * rows + r0 + i, epoch, v);

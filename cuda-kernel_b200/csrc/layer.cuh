@@ -165,43 +165,41 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
     griddep_wait();  // x may be the previous kernel's output
     // Tensor parallel: every CTA reads this call's exchange epoch before it reaches
     // the grid barrier; CTA 0 stores it after the barrier.
-    const uint32_t xe = (TP && t == 0) ? next_epoch(*reinterpret_cast<volatile const uint32_t*>(tp.ctr)) : 0u;
+    const uint32_t xe0 = (TP && t == 0) ? *reinterpret_cast<volatile const uint32_t*>(tp.ctr) : 0u;
     float xr[kLayerMaxJ][8];
     int s = 0;
     uint32_t ph = 0;
 
     // ---- phase 1: gate rows [a0, a1)
     load_slice<CT>(L.x, L.hidden, t, false, xr);
-    {
-        const int nv = L.hidden / 8;
-        for (int k = 0; k < units1; ++k) {
+    // Both phases reduce RG rows at once (stage_rows); RG is chosen from the
+    // vectors per thread, once per phase, so each loop keeps only the part of
+    // xr it reads in registers.
+    auto phase = [&](auto nm, auto rg, auto jv, int units, int base, int first, int last, int rsx, int cols,
+                     float* part) {
+        constexpr int NM = decltype(nm)::value, RG = decltype(rg)::value, J = decltype(jv)::value;
+        const int nv = cols / 8;
+        for (int k = 0; k < units; ++k) {
             if (!mbar_wait(smem_u32(full + s), ph)) { s_failed = 1; break; }
-            const int row0 = a0 + k * L.rs1;
-            const int ru = min(L.rs1, a1 - row0);
+            const int row0 = first + k * rsx;
+            const int ru = min(rsx, last - row0);
             const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
-            for (int r = 0; r < ru; ++r) {
-                float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-                const __half* wrow = sw + size_t(r) * L.hidden;
-                const __half* urow = wrow + size_t(L.rs1) * L.hidden;
-#pragma unroll
-                for (int j = 0; j < kLayerMaxJ; ++j) {
-                    const int v = t + j * CT;
-                    if (v < nv) {
-                        dot8(*reinterpret_cast<const uint4*>(wrow + size_t(v) * 8), xr[j], acc[0]);
-                        dot8(*reinterpret_cast<const uint4*>(urow + size_t(v) * 8), xr[j], acc[1]);
-                    }
-                }
-                const float ga = warp_sum(fold4(acc[0]));
-                const float ub = warp_sum(fold4(acc[1]));
-                if (lane == 0) {
-                    part1[(size_t(row0 - a0 + r) * CW + warp) * 2] = ga;
-                    part1[(size_t(row0 - a0 + r) * CW + warp) * 2 + 1] = ub;
-                }
-            }
+            stage_rows<CW, kLayerMaxJ, NM, RG, J>(sw, ru, rsx, cols, nv, xr, part, row0 - base);
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(empty + s));
             if (++s == stages) { s = 0; ph ^= 1u; }
         }
+    };
+    using I1 = std::integral_constant<int, 1>;
+    using I2 = std::integral_constant<int, 2>;
+    using I4 = std::integral_constant<int, 4>;
+    using I8 = std::integral_constant<int, 8>;
+    using IJ = std::integral_constant<int, kLayerMaxJ>;
+    {
+        const int jn = (L.hidden / 8 + CT - 1) / CT;
+        if (jn <= 1) phase(I2{}, I4{}, I1{}, units1, a0, a0, a1, L.rs1, L.hidden, part1);
+        else if (jn <= 2) phase(I2{}, I2{}, I2{}, units1, a0, a0, a1, L.rs1, L.hidden, part1);
+        else phase(I2{}, I1{}, IJ{}, units1, a0, a0, a1, L.rs1, L.hidden, part1);
     }
     named_barrier_sync(1, CT);
     if (s_failed) return;
@@ -237,6 +235,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
         }
         __threadfence();
     }
+    const uint32_t xe = xe0 + 1u;  // this call's epoch (read before the barrier, used after it)
     if (TP && b == 0 && t == 0) *reinterpret_cast<volatile uint32_t*>(tp.ctr) = xe;
     named_barrier_sync(1, CT);
     if (!s_ok) return;
@@ -244,27 +243,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
     // ---- phase 2: down rows [d0, d1) against h
     load_slice<CT>(L.h, L.inter, t, true, xr);
     {
-        const int nv = L.inter / 8;
-        for (int k = 0; k < units2; ++k) {
-            if (!mbar_wait(smem_u32(full + s), ph)) { s_failed = 1; break; }
-            const int row0 = d0 + k * L.rs2;
-            const int ru = min(L.rs2, d1 - row0);
-            const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
-            for (int r = 0; r < ru; ++r) {
-                float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                const __half* wrow = sw + size_t(r) * L.inter;
-#pragma unroll
-                for (int j = 0; j < kLayerMaxJ; ++j) {
-                    const int v = t + j * CT;
-                    if (v < nv) dot8(*reinterpret_cast<const uint4*>(wrow + size_t(v) * 8), xr[j], acc);
-                }
-                const float a = warp_sum(fold4(acc));
-                if (lane == 0) part2[size_t(row0 - d0 + r) * CW + warp] = a;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(empty + s));
-            if (++s == stages) { s = 0; ph ^= 1u; }
-        }
+        const int jn = (L.inter / 8 + CT - 1) / CT;
+        if (jn <= 1) phase(I1{}, I8{}, I1{}, units2, d0, d0, d1, L.rs2, L.inter, part2);
+        else if (jn <= 2) phase(I1{}, I4{}, I2{}, units2, d0, d0, d1, L.rs2, L.inter, part2);
+        else phase(I1{}, I1{}, IJ{}, units2, d0, d0, d1, L.rs2, L.inter, part2);
     }
     named_barrier_sync(1, CT);
     if (s_failed) return;

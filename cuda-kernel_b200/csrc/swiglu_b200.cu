@@ -217,6 +217,9 @@ int launch_rbulk(Params p, cudaStream_t stream, bool pdl) {
         if (stages >= 2 || rs == 1) break;
     }
     if (!ok || rs < 1 || stages < 2) return dispatch_fallback<MODE>(SWB_RBULK_FALLBACK_ID, p, stream, pdl);
+    // no deeper than the CTA's stages of work: a short shard then leaves shared
+    // memory for the next kernel's CTAs to become resident early
+    stages = std::min(stages, std::max(2, (rows_per_cta + rs - 1) / rs));
     p.stages = stages;
     p.row_stage = rs;
     const size_t smem = rbulk_layout(NM, rs, p.cols, stages, CW, rows_per_cta).total;
@@ -252,6 +255,7 @@ int launch_rbulk_ar(Params p, const TpParams& tp, cudaStream_t stream, bool pdl)
         if (stages >= 2 || rs == 1) break;
     }
     if (rs < 1 || stages < 2) return fail(SWB_E_UNSUPPORTED, "shape does not fit the geometry's shared memory");
+    stages = std::min(stages, std::max(2, (rows_per_cta + rs - 1) / rs));  // as launch_rbulk
     p.stages = stages;
     p.row_stage = rs;
     const size_t smem = rbulk_layout(1, rs, p.cols, stages, CW, rows_per_cta).total;

@@ -199,6 +199,7 @@ def rbulk_plan(cfg, rows, cols, gated, w_aligned=True):
         rs = rs // 2 if rs > 1 else 0
     if not ok or rs < 1 or stages < 2:
         return None
+    stages = min(stages, max(2, (rpc + rs - 1) // rs))  # no deeper than a CTA's stages of work
     return {"G": G, "rpc": rpc, "rs": rs, "stages": stages, "budget": budget,
             "layout": rbulk_layout(nm, rs, cols, stages, cw, rpc)}
 
