@@ -485,17 +485,47 @@ __host__ __device__ inline BulkLayout rbulk_layout(int nm, int row_stage, int co
     return L;
 }
 
+// Sums K values (K a power of two, at most 32) over the 32 lanes of a warp.
+// Each of the first log2(K) xor steps halves what a lane carries: the lane
+// keeps one half of its values, sends the other half to its partner and adds
+// what comes back; a plain butterfly over the remaining lane bits finishes. K
+// values cost K/2 + K/4 + ... + 1 + (5 - log2 K) shuffles (9 for K = 8) instead
+// of 5K, which matters when many warps of an SM reduce short rows at once.
+// Lane L returns the total of value (L >> (5 - log2 K)); the order of the adds
+// is fixed, so the result is deterministic.
+template <int K>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[K], int lane) {
+    static_assert(K >= 1 && K <= 32 && (K & (K - 1)) == 0, "K must be a power of two up to 32");
+#pragma unroll
+    for (int k = K, d = 16; k > 1; k >>= 1, d >>= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < k / 2; ++i) {
+            const float send = upper ? v[i] : v[i + k / 2];
+            const float keep = upper ? v[i + k / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+    }
+    constexpr int LK = K >= 32 ? 5 : K >= 16 ? 4 : K >= 8 ? 3 : K >= 4 ? 2 : K >= 2 ? 1 : 0;
+    float t = v[0];
+#pragma unroll
+    for (int d = 16 >> LK; d; d >>= 1) t += __shfl_xor_sync(0xffffffffu, t, d);
+    return t;
+}
+
 // Dot products of the `ru` rows of one ring stage with the consumer's register
-// slice xr (vectors t + j*CT, j < J), RG rows at a time: the RG butterfly
-// reductions run interleaved, so rows that give each thread only a vector or two
-// are not bound by one dependent shuffle chain per row. Each row's result is the
-// same xor butterfly as warp_sum's. Lane 0 stores the warp partials of row
-// prow0 + r into part[row][warp][matrix].
+// slice xr (vectors t + j*CT, j < J), RG rows at a time: the RG * NM row sums of
+// a group are reduced together (warp_reduce_scatter), so rows that give each
+// thread only a vector or two are bound neither by one dependent shuffle chain
+// per row nor by the SM's shuffle throughput. The lane holding a row's sum
+// stores the warp partial of row prow0 + r into part[row][warp][matrix].
 template <int CW, int MAXJ, int NM, int RG, int J>
 __device__ __forceinline__ void stage_rows(const __half* sw, int ru, int rs, int cols, int nv, const float (&xr)[MAXJ][8],
                                            float* part, int prow0) {
     static_assert(J <= MAXJ, "vectors per thread");
     constexpr int CT = CW * 32;
+    constexpr int K = RG * NM;
+    constexpr int LK = K >= 32 ? 5 : K >= 16 ? 4 : K >= 8 ? 3 : K >= 4 ? 2 : K >= 2 ? 1 : 0;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     for (int r = 0; r < ru; r += RG) {
         float acc[RG][NM][4];
@@ -520,38 +550,20 @@ __device__ __forceinline__ void stage_rows(const __half* sw, int ru, int rs, int
                 }
             }
         }
-        float red[RG][NM];
+        float red[K];
 #pragma unroll
         for (int g = 0; g < RG; ++g)
 #pragma unroll
-            for (int m = 0; m < NM; ++m) red[g][m] = fold4(acc[g][m]);
-#pragma unroll
-        for (int d = 16; d; d >>= 1)
-#pragma unroll
-            for (int g = 0; g < RG; ++g)
-#pragma unroll
-                for (int m = 0; m < NM; ++m) red[g][m] += __shfl_xor_sync(0xffffffffu, red[g][m], d);
-        if (lane == 0) {
-#pragma unroll
-            for (int g = 0; g < RG; ++g)
-                if (r + g < ru)
-#pragma unroll
-                    for (int m = 0; m < NM; ++m) part[(size_t(prow0 + r + g) * CW + warp) * NM + m] = red[g][m];
+            for (int m = 0; m < NM; ++m) red[g * NM + m] = fold4(acc[g][m]);
+        const float total = warp_reduce_scatter<K>(red, lane);
+        if ((lane & ((32 >> LK) - 1)) == 0) {
+            const int idx = lane >> (5 - LK);
+            const int g = idx / NM, m = idx % NM;
+            if (r + g < ru) part[(size_t(prow0 + r + g) * CW + warp) * NM + m] = total;
         }
     }
 }
 
-
-// Persistent row-stage streaming. CTA b owns rows [b*rows/G, (b+1)*rows/G).
-// A producer thread streams them with one cp.async.bulk per matrix per ring
-// stage; a stage holds `row_stage` whole rows, which are contiguous in a
-// row-major matrix. Consumer thread t owns the 16-byte vectors t + j*CT (j <
-// MAXJ) of EVERY row, so its slice of x is loaded once into registers and the
-// only shared-memory traffic is the weights themselves (written by the copy
-// engine, read once by the consumers). Row sums: a warp reduction per row into
-// a fixed slot of `part`; `finish(r0, nrows, part)` then runs on the consumer
-// threads (after a consumer barrier) to combine the warps and write the rows.
-// Returns false on the producer warp and when a bounded wait gave up.
 template <int CW, int MAXJ, int MODE>
 __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* smem, int& r0_out, int& nrows_out,
                                              float*& part_out, uint32_t* epoch_out = nullptr) {

@@ -91,7 +91,6 @@ int sm_count() {
 // Raises a kernel's dynamic shared-memory limit once per device.
 template <typename Kernel>
 int ensure_smem(Kernel kernel, std::atomic<uint64_t>& done_mask, size_t bytes) {
-    if (bytes <= 48 * 1024) return SWB_OK;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return check_launch();
     const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
@@ -101,8 +100,17 @@ int ensure_smem(Kernel kernel, std::atomic<uint64_t>& done_mask, size_t bytes) {
     cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
     if (bytes + fa.sharedSizeBytes > kSmemPerCtaMax) return fail(SWB_E_CUDA, "shared memory request too large");
+    // the permitted maximum, once per kernel and device, whatever this request needs
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(kSmemPerCtaMax - fa.sharedSizeBytes));
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    // Every kernel asks for the largest shared-memory carveout, so all of them
+    // run in one SM configuration: CTAs of the next kernel (the down projection,
+    // launched programmatically) can join an SM beside the gate's CTAs and start
+    // streaming their weights, instead of waiting for the SM to drain and be
+    // reconfigured for a different L1 / shared split.
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared));
     if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
     if (bit) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return SWB_OK;
