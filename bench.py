@@ -363,7 +363,7 @@ def ours(args) -> None:
     # atol_j: the change one fp16 rounding of h can make in y_j (h is fp16 by contract)
     atol = 2.0 ** -11 * (w0["wd"].float().abs() @ href.float().abs())
     rel = ((y - yref).abs() / (yref.abs() + atol)).max().item()
-    del w0, gref, uref, href, yref, atol
+    del w0, gref, uref, href, yref
     if world > 1:  # every rank takes the same exit decision
         t = torch.tensor([rel], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -371,13 +371,17 @@ def ours(args) -> None:
     if not rel <= 2e-3:
         raise SystemExit(f"bench sanity check failed: max relative error {rel}")
     if world > 1:  # the NCCL baseline must agree with the fused path too
+        # Both sum the same fp32 partials, in different orders: they differ by a few
+        # ulps of sum_i |Wd[j,i] h_i| = 2^11 atol_j. A missing or doubled partial would
+        # be off by about that sum / N, orders of magnitude above the bound.
         y_fused = y.clone()
         step_nccl(0)
         torch.cuda.synchronize()
-        dn = ((y - y_fused).abs() / (y_fused.abs() + 1e-6)).max()
+        dn = ((y - y_fused).abs() / (y_fused.abs() + atol)).max()
         dist.all_reduce(dn, op=dist.ReduceOp.MAX)
-        if not float(dn) <= 1e-5:
+        if not float(dn) <= 2e-3:  # the tolerance of the check against the fp32 reference above
             raise SystemExit(f"fused and NCCL tensor-parallel paths disagree: {float(dn)}")
+    del atol
     launches_per_step = 1 if lcfg else 2
 
     # ---- one CUDA graph per rotating copy holds the whole step (as the reference
