@@ -132,7 +132,8 @@ SWB_API int swb_ffn_noalloc(int gate_config, int down_config, const void* wg, co
  * layer_config is a layer id (swb_layer_config_ids); a geometry that cannot hold
  * a row of the shape falls back to 200, then 203. Needs hidden and inter
  * multiples of 8 and 16-byte aligned weights (else SWB_E_UNSUPPORTED: use swb_ffn).
- * The launch is cooperative: every CTA must be resident at once. */
+ * The launch is cooperative: every CTA must be resident at once. After a device
+ * error (swb_device_error) zero the workspace again before the next call. */
 #define SWB_LAYER_WORKSPACE_BYTES 8192
 SWB_API int swb_layer_config_count(void);
 SWB_API int swb_layer_config_ids(int* out, int cap);
@@ -162,7 +163,8 @@ SWB_API int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, c
  * swb_tp_ipc_handle with every rank (any transport), swb_tp_connect with all
  * handles in rank order. Every rank must then make the same sequence of
  * swb_ffn_tp_fused calls with the same shapes and geometries (one exchange per
- * stream of calls; calls on one exchange must not overlap). */
+ * stream of calls; calls on one exchange must not overlap). After a device error
+ * (swb_device_error) destroy and recreate the exchange on every rank. */
 #define SWB_DEVERR_PEER_TIMEOUT 2
 #define SWB_TP_MAX_RANKS 8
 #define SWB_TP_HANDLE_BYTES 64
