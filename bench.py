@@ -13,7 +13,11 @@ twice the 126 MB L2, so every step streams its weights from HBM.
   intermediate row, Wd by its K dimension; the down kernel sums the ranks'
   partial y over NVLink peer memory and adds bias + residual once (fused
   all-reduce). The NCCL all-reduce path is timed beside it as the baseline.
-  Each rank's step is captured in a CUDA graph.
+
+Steps are captured in CUDA graphs: the timed steps run as graphs that each hold
+one step per rotating weight copy back to back (as the layers of a decode step);
+the reference's protocol, one step per graph replay, is timed and reported
+beside it (``one_step_graph_us``), and so are the baselines.
 
 Prints ONE JSON line on rank 0. ``--impl reference`` times the reference's own
 CPU path (its include/contract.hpp matvec, compiled under oracle/_ref) on the
@@ -48,6 +52,8 @@ def parse():
     p.add_argument("--intermediate", type=int, default=14336)
     p.add_argument("--gate-config", type=int, default=0, help="registry id (0 = tune)")
     p.add_argument("--down-config", type=int, default=0, help="registry id (0 = tune)")
+    p.add_argument("--graph-steps", type=int, default=0,
+                   help="layer steps per CUDA graph (0 = one per rotating weight copy, 1 = one step per graph)")
     p.add_argument("--layer-config", type=int, default=0,
                    help="fused whole-layer kernel id (0 = tune against the two-kernel path, -1 = never)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
@@ -384,32 +390,50 @@ def ours(args) -> None:
     del atol
     launches_per_step = 1 if lcfg else 2
 
-    # ---- one CUDA graph per rotating copy holds the whole step (as the reference
-    # times its candidates: src/benchmark.cu:46-83); for N > 1 it includes the NCCL all-reduce
+    # ---- CUDA graphs. One graph per rotating copy holds one whole step (the reference's
+    # protocol: src/benchmark.cu:46-83, one captured call replayed); the timed steps are
+    # issued as graphs that each hold `chain` consecutive steps, one per weight copy, as the
+    # layers of a decode step run back to back in one graph. Every step still does all of
+    # its work; `one_step_graph_us` reports the one-step-per-graph protocol beside it.
+    chain = args.graph_steps if args.graph_steps > 0 else copies
+    chain = max(1, min(chain, copies))
+
+    def capture(fn, first, n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for k in range(n):
+                fn((first + k) % copies)
+        return g
+
     for c in range(copies):
         step(c)  # warm every copy (and NCCL) before capture
     torch.cuda.synchronize()
-    graphs = []
-    for c in range(copies):
-        graphs.append(torch.cuda.CUDAGraph())
-        with torch.cuda.graph(graphs[-1], stream=stream):
-            step(c)
+    graphs = [capture(step, c, 1) for c in range(copies)]
+    chained = [capture(step, 0, chain)] if chain > 1 else []
     torch.cuda.synchronize()
+
+    def run_steps(n, one_per_graph=False):
+        # n steps in order: whole chains first, then single-step graphs for the rest
+        i = 0
+        if chained and not one_per_graph:
+            for _ in range(n // chain):
+                chained[0].replay()
+            i = (n // chain) * chain
+        for k in range(i, n):
+            graphs[k % copies].replay()
 
     def run_step(i):
         graphs[i % copies].replay()
 
     sampler = ClockSampler(local, interval_s=0.002).start()
-    for i in range(args.warmup):
-        run_step(i)
+    run_steps(max(args.warmup, chain))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_window = [time.time()]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for i in range(args.steps):
-        run_step(i)
+    run_steps(args.steps)
     end.record(stream)
     end.synchronize()
     t_window.append(time.time())
@@ -427,13 +451,20 @@ def ours(args) -> None:
     if elapsed_ms < 300.0:
         soak_steps = int(math.ceil(300.0 / max(elapsed_ms, 1e-3) * args.steps))
         t0 = time.time()
-        for i in range(soak_steps):
-            run_step(i)
+        run_steps(soak_steps)
         torch.cuda.synchronize()
         soak_window = (t0, time.time())
         if world > 1:
             dist.barrier()
     us_per_layer = elapsed_ms * 1e3 / args.steps
+    # the reference's protocol: the same steps, one step per graph replay (max over ranks)
+    if world > 1:
+        dist.barrier()
+    one_step_us = time_kernel(torch, lambda i: run_step(i), args.steps, stream)
+    if world > 1:
+        t = torch.tensor([one_step_us], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        one_step_us = float(t.item())
 
     # ---- dominant kernel: CUDA events around each launch, same rotating copies. With the
     # fused layer kernel that is the one launch of the step; otherwise the gate kernel.
@@ -471,25 +502,27 @@ def ours(args) -> None:
     # ---- all-reduce alone (tensor parallel): reported separately, it is latency-bound
     tp = None
     if world > 1:
-        # the NCCL baseline step, captured and timed the same way (max over ranks)
-        ngraphs = []
+        # the NCCL baseline step, captured and timed the same two ways (max over ranks)
         for c in range(copies):
             step_nccl(c)
         torch.cuda.synchronize()
-        for c in range(copies):
-            ngraphs.append(torch.cuda.CUDAGraph())
-            with torch.cuda.graph(ngraphs[-1], stream=stream):
-                step_nccl(c)
+        ngraphs = [capture(step_nccl, c, 1) for c in range(copies)]
+        nchain = capture(step_nccl, 0, chain) if chain > 1 else None
         for i in range(args.warmup):
             ngraphs[i % copies].replay()
         dist.barrier()
-        nccl_us = time_kernel(torch, lambda i: ngraphs[i % copies].replay(), args.steps, stream)
+        nccl_one = time_kernel(torch, lambda i: ngraphs[i % copies].replay(), args.steps, stream)
+        nccl_us = nccl_one
+        if nchain is not None and args.steps >= chain:
+            dist.barrier()
+            nccl_us = time_kernel(torch, lambda i: nchain.replay(), args.steps // chain, stream) / chain
+            nchain.reset()
         for gr in ngraphs:
             gr.reset()
         ngraphs.clear()
-        t = torch.tensor([nccl_us], dtype=torch.float64, device=device)
+        t = torch.tensor([nccl_us, nccl_one], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        nccl_us = float(t.item())
+        nccl_us, nccl_one = float(t[0]), float(t[1])
         # 20 all-reduces captured in one graph, replayed: device-side latency, not host launch rate
         ag = torch.cuda.CUDAGraph()
         with torch.cuda.graph(ag, stream=stream):
@@ -504,6 +537,7 @@ def ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         tp = {"ranks": world, "shard_rows": shard, "exchange": "fused one-shot all-reduce over NVLink peer memory "
               "in the down kernel", "nccl_step_us": nccl_us, "fused_speedup_vs_nccl": nccl_us / us_per_layer,
+              "nccl_one_step_graph_us": nccl_one,
               "nccl_allreduce_us": float(t.item()), "allreduce_bytes": H * 4}
 
     # ---- end to end through the public C-ABI call with host buffers (N=1). As the
@@ -579,29 +613,33 @@ def ours(args) -> None:
         ubuf = torch.empty_like(gbuf)
         hb = torch.empty(I, dtype=torch.float16, device=device)
         yb = torch.empty(H, dtype=torch.float32, device=device)
-        res = {}
+        res, res_one = {}, {}
         for algo in (0, 1):
-            # warm (cuBLAS workspaces), capture one graph per copy, time replays -- the same
-            # protocol as our layer (src/benchmark.cu:46-83)
-            cg = []
-            for c in range(copies):
+            # warm (cuBLAS workspaces), capture and time replays -- the same two protocols as
+            # our layer: chained steps per graph, and one step per graph (src/benchmark.cu:46-83)
+            def cstep(c, algo=algo):
                 base.ffn(x, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, gbuf, ubuf, hb, yb, algo=algo,
                          stream=sp)
-            torch.cuda.synchronize()
             for c in range(copies):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    base.ffn(x, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, gbuf, ubuf, hb, yb,
-                             algo=algo, stream=sp)
-                cg.append(g)
+                cstep(c)
+            torch.cuda.synchronize()
+            cg = [capture(cstep, c, 1) for c in range(copies)]
             fn = lambda i, cg=cg: cg[i % copies].replay()  # noqa: E731
             for i in range(args.warmup):
                 fn(i)
-            res[algo] = time_kernel(torch, fn, args.steps, stream)
-            del cg
+            res_one[algo] = time_kernel(torch, fn, args.steps, stream)
+            res[algo] = res_one[algo]
+            if chain > 1 and args.steps >= chain:
+                cc = capture(cstep, 0, chain)
+                cc.replay()
+                res[algo] = time_kernel(torch, lambda i: cc.replay(), args.steps // chain, stream) / chain
+                cc.reset()
+            for g in cg:
+                g.reset()
         algo = min(res, key=res.get)
         cublas = {"value": res[algo], "unit": UNIT, "algo": ["default", "default_tensor_op"][algo],
-                  "kernels_per_step": 5, "speedup_vs_cublas": res[algo] / us_per_layer}
+                  "kernels_per_step": 5, "speedup_vs_cublas": res[algo] / us_per_layer,
+                  "one_step_graph_us": res_one[algo], "speedup_vs_cublas_one_step_graph": res_one[algo] / one_step_us}
         base.close()
 
     clocks = sampler.stop(window=tuple(t_window), fallback_window=soak_window)
@@ -612,11 +650,14 @@ def ours(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": us_per_layer, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "one_step_graph_us": one_step_us,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
                        "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
                        "layer_config": lcfg or None,
+                       "graph": f"{chain} consecutive steps (one per weight copy) per CUDA graph replay"
+                                if chain > 1 else "one step per CUDA graph replay",
                        "rotating_copies": copies,
                        "l2": f"inputs larger than L2: {copies} rotating weight copies of "
                              f"{weight_bytes_rank / 2**20:.0f} MiB per rank",
@@ -636,9 +677,10 @@ def ours(args) -> None:
 
     # Release every graph (some hold NCCL all-reduces) before the process group goes.
     torch.cuda.synchronize()
-    for gr in graphs:
+    for gr in graphs + chained:
         gr.reset()
     graphs.clear()
+    chained.clear()
     if world > 1:
         dist.barrier()
         torch.cuda.synchronize()
