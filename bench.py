@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--down-config", type=int, default=0, help="registry id (0 = tune)")
     p.add_argument("--graph-steps", type=int, default=0,
                    help="layer steps per CUDA graph (0 = one per rotating weight copy, 1 = one step per graph)")
+    p.add_argument("--no-prefetch-weights", action="store_true",
+                   help="launch each step's gate in plain stream order (no SWB_PREFETCH_WEIGHTS)")
     p.add_argument("--layer-config", type=int, default=0,
                    help="fused whole-layer kernel id (0 = tune against the two-kernel path, -1 = never)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
@@ -285,6 +287,10 @@ def ours(args) -> None:
         exchange = Exchange(rank, world, H, device)  # one-time set-up: IPC handles shared by all_gather
     workspace = binding.layer_workspace(device)  # grid-barrier slots of the one-GPU fused layer kernel
 
+    # The weights are written once, before any step: each step's gate may start streaming them
+    # while the previous step's down kernel (and exchange) still runs (SWB_PREFETCH_WEIGHTS).
+    flags = 0 if args.no_prefetch_weights else _lib.SWB_PREFETCH_WEIGHTS
+
     def layer_step(cfg, g, d, i):
         # cfg = 0: gate kernel, then the down kernel launched programmatically (for N > 1 the
         # down kernel also sums the ranks' partials over NVLink); cfg > 0: the whole layer
@@ -295,13 +301,14 @@ def ours(args) -> None:
                                        x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
                                        y.data_ptr(), H, shard, workspace.data_ptr(), sp))
         elif world == 1:
-            _lib.check(L.swb_ffn(g, d, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
-                                 x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
-                                 y.data_ptr(), H, shard, sp))
+            _lib.check(L.swb_ffn_ex(g, d, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                    x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
+                                    y.data_ptr(), H, shard, flags, sp))
         else:
-            _lib.check(L.swb_ffn_tp_fused(exchange.handle, cfg or g, 0 if cfg else d, s["wg"].data_ptr(),
-                                          s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(),
-                                          bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard, sp))
+            _lib.check(L.swb_ffn_tp_fused_ex(exchange.handle, cfg or g, 0 if cfg else d, s["wg"].data_ptr(),
+                                             s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(),
+                                             bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard,
+                                             flags, sp))
 
     def median_step_us(fn):
         torch.cuda.synchronize()
@@ -656,6 +663,7 @@ def ours(args) -> None:
             "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
                        "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
                        "layer_config": lcfg or None,
+                       "prefetch_weights": bool(flags),
                        "graph": f"{chain} consecutive steps (one per weight copy) per CUDA graph replay"
                                 if chain > 1 else "one step per CUDA graph replay",
                        "rotating_copies": copies,

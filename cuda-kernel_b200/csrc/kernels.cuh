@@ -52,11 +52,12 @@ struct Params {
     uint32_t* epoch;
 };
 
-// First thing in every kernel that can run as the gate of a tensor-parallel call:
-// one fire-and-forget add (no thread waits for it). The previous call's down
-// kernel, which read the epoch, completed before this gate started (the gate is
-// launched in stream order); this call's down kernel reads it only after
-// griddepcontrol.wait, when this grid's memory operations are complete. Epochs
+// In every kernel that can run as the gate of a tensor-parallel call, right after
+// its griddepcontrol.wait: one fire-and-forget add (no thread waits for it). The
+// previous call's down kernel, which read the epoch, has completed by then (even
+// when the gate was launched programmatically and started early); this call's
+// down kernel reads it only after its own griddepcontrol.wait, when this grid's
+// memory operations are complete. Epochs
 // start at 1 in a zeroed exchange, so a slot's epoch field is 0 only until its
 // first write; every call writes each slot a reader of its parity waits on, so
 // when the counter wraps back to 0 no such slot still holds that value.
@@ -184,7 +185,6 @@ __device__ __forceinline__ void stage_x(const __half* __restrict__ x, float* xs,
 
 template <int WPR, int ROWS, int PACK, int UNROLL, int MODE>
 __global__ void __launch_bounds__(32 * WPR * ROWS) ldg_kernel(const Params p) {
-    advance_call_epoch(p);
     static_assert(WPR > 0 && (WPR & (WPR - 1)) == 0 && ROWS > 0 && 32 * WPR * ROWS <= 1024, "geometry");
     static_assert(PACK == 2 || PACK == 8, "pack");
     constexpr bool GATED = MODE == MODE_GATE;
@@ -200,6 +200,7 @@ __global__ void __launch_bounds__(32 * WPR * ROWS) ldg_kernel(const Params p) {
     griddep_launch_dependents();
     // x may be the previous kernel's output (h of the gate stage).
     griddep_wait();
+    advance_call_epoch(p);
     if (p.x_staged) {
         stage_x(p.x, xs, cols, threadIdx.x, blockDim.x);
         __syncthreads();
@@ -336,7 +337,6 @@ __host__ __device__ inline BulkLayout bulk_layout(int nm, int chunk, int stages,
 
 template <int CW, int CHUNK, int MODE>
 __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) {
-    advance_call_epoch(p);
     static_assert(CHUNK % 8 == 0 && CHUNK > 0, "chunk must be whole 16-byte vectors");
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
@@ -409,6 +409,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
+    advance_call_epoch(p);
     stage_x(p.x, xs, cols, t, CT);
     named_barrier_sync(1, CT);
     float acc[NM][4];
@@ -637,8 +638,13 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
-    // the call epoch the gate kernel advanced (fused tensor-parallel down only)
-    if (epoch_out && t == 0) *epoch_out = *reinterpret_cast<volatile const uint32_t*>(p.epoch);
+    // the fused tensor-parallel down kernel reads the call epoch its gate advanced;
+    // as the gate of a tensor-parallel call this kernel advances it
+    if (epoch_out) {
+        if (t == 0) *epoch_out = *reinterpret_cast<volatile const uint32_t*>(p.epoch);
+    } else {
+        advance_call_epoch(p);
+    }
     float xr[MAXJ][8];
     const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
 #pragma unroll
@@ -705,7 +711,6 @@ __device__ __forceinline__ float row_sum(const float* part, int i, int m) {
 
 template <int CW, int MAXJ, int CPS, int MODE>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params p) {
-    advance_call_epoch(p);
     constexpr int NM = MODE == MODE_GATE ? 2 : 1;
     constexpr int CT = CW * 32;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -831,7 +836,6 @@ __host__ __device__ inline StealLayout sbulk_layout(int nm, int row_stage, int c
 // deterministic whatever the stealing order.
 template <int CW, int MAXJ, int CPS, int MODE>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params p) {
-    advance_call_epoch(p);
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
     constexpr int CT = CW * 32;
@@ -966,6 +970,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
+    advance_call_epoch(p);
     float xr[MAXJ][8];
     const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
 #pragma unroll

@@ -570,7 +570,7 @@ namespace {
 // swb_gate; `epoch` (tensor parallel) is the exchange's call epoch, which the
 // kernel advances for the fused down kernel that follows.
 int gate_impl(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu, void* h,
-              int rows, int cols, int model_round, void* stream, uint32_t* epoch) {
+              int rows, int cols, int model_round, void* stream, uint32_t* epoch, bool pdl = false) {
     if (rows <= 0 || cols <= 0 || !wg || !x) return fail(SWB_E_INPUT);
     if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
     if (!find_config(config)) return fail(SWB_E_CONFIG);
@@ -585,7 +585,7 @@ int gate_impl(int config, const void* wg, const void* wu, const void* x, const v
     p.rows = rows;
     p.cols = cols;
     p.model_round = model_round ? 1 : 0;
-    return dispatch<MODE_GATE>(config, p, static_cast<cudaStream_t>(stream));
+    return dispatch<MODE_GATE>(config, p, static_cast<cudaStream_t>(stream), pdl);
 }
 }  // namespace
 
@@ -630,10 +630,19 @@ int swb_project(int config, const void* w, const void* x, const void* bias, cons
 int swb_ffn(int gate_config, int down_config, const void* wg, const void* wu, const void* wd, const void* x,
             const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
             void* stream) {
+    return swb_ffn_ex(gate_config, down_config, wg, wu, wd, x, bg, bu, bd, h, y, hidden, inter, 0u, stream);
+}
+
+int swb_ffn_ex(int gate_config, int down_config, const void* wg, const void* wu, const void* wd, const void* x,
+               const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
+               unsigned flags, void* stream) {
+    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
     if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
     if (!wd) return fail(SWB_E_INPUT);
     if (!y) return fail(SWB_E_FLOAT_OUTPUT);
-    if (int rc = swb_gate(gate_config, wg, wu, x, bg, bu, h, inter, hidden, 0, stream)) return rc;
+    if (int rc = gate_impl(gate_config, wg, wu, x, bg, bu, h, inter, hidden, 0, stream, nullptr,
+                           (flags & SWB_PREFETCH_WEIGHTS) != 0))
+        return rc;
     return project_impl(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream, true);
 }
 
@@ -838,6 +847,15 @@ int swb_tp_destroy(swb_tp_t* tp) {
 int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
                      const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard, const void* bd,
                      void* h_shard, float* y, int hidden, int shard, void* stream) {
+    return swb_ffn_tp_fused_ex(tp, gate_config, down_config, wg_shard, wu_shard, wd_shard, x, bg_shard, bu_shard, bd,
+                               h_shard, y, hidden, shard, 0u, stream);
+}
+
+int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
+                        const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard,
+                        const void* bd, void* h_shard, float* y, int hidden, int shard, unsigned flags,
+                        void* stream) {
+    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
     if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
     if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
     const bool layer = is_layer_config(gate_config);
@@ -864,7 +882,7 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
     const TpParams t = tp_params(tp, bd, x);
     // the gate kernel advances the call epoch; the down kernel reads it after griddepcontrol.wait
     if (int rc = gate_impl(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream,
-                           t.ctr))
+                           t.ctr, (flags & SWB_PREFETCH_WEIGHTS) != 0))
         return rc;
     Params p = make_params();
     p.w = static_cast<const __half*>(wd_shard);

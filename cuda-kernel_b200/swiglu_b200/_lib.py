@@ -41,6 +41,7 @@ SWB_TP_MAX_RANKS = 8
 SWB_LAYER_WORKSPACE_BYTES = 8192
 SWB_TP_HANDLE_BYTES = 64
 SWB_DEVERR_PEER_TIMEOUT = 2
+SWB_PREFETCH_WEIGHTS = 1
 SWB_RESIDUAL = 1
 SWB_HALF_OUT = 2
 SWB_FAMILY_LDG = 0
@@ -90,6 +91,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_gate": ([_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
         "swb_project": ([_i, _vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.c_uint, _vp], _i),
         "swb_ffn": ([_i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "swb_ffn_ex": ([_i, _i] + [_vp] * 9 + [_i, _i, ctypes.c_uint, _vp], _i),
         "swb_ffn_tp": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_ffn_noalloc": ([_i, _i] + [_vp] * 8 + [_i, _i, _vp], _i),
         "swb_layer_config_count": ([], _i),
@@ -101,6 +103,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_tp_connect": ([_vp, _vp], _i),
         "swb_tp_destroy": ([_vp], _i),
         "swb_ffn_tp_fused": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, _vp], _i),
+        "swb_ffn_tp_fused_ex": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, ctypes.c_uint, _vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),
         "swb_residual_epilogue": ([_vp, _vp, _vp, _i, _vp], _i),
         "swb_device_error": ([_i, ctypes.POINTER(_i)], _i),

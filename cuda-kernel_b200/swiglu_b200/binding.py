@@ -131,14 +131,19 @@ def project(w: torch.Tensor, x: torch.Tensor, out: torch.Tensor, config: int,
 
 def ffn(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, bg: torch.Tensor,
         bu: torch.Tensor, bd: torch.Tensor, h: torch.Tensor, y: torch.Tensor, gate_config: int,
-        down_config: int, stream: int | None = None) -> None:
-    """Whole layer with biases and residual (benchmark.cu:161-165): y fp32 [H]."""
+        down_config: int, stream: int | None = None, prefetch_weights: bool = False) -> None:
+    """Whole layer with biases and residual (benchmark.cu:161-165): y fp32 [H].
+
+    ``prefetch_weights``: SWB_PREFETCH_WEIGHTS -- the gate may start streaming Wg/Wu
+    before the previous kernel in the stream finishes (no kernel before the call may
+    write them)."""
     inter, hidden = wg.shape
     s = _stream(x.device) if stream is None else stream
+    flags = _lib.SWB_PREFETCH_WEIGHTS if prefetch_weights else 0
     with torch.cuda.device(x.device):
-        _lib.check(_lib.lib().swb_ffn(int(gate_config), int(down_config), wg.data_ptr(), wu.data_ptr(),
-                                      wd.data_ptr(), x.data_ptr(), _ptr(bg), _ptr(bu), _ptr(bd), h.data_ptr(),
-                                      y.data_ptr(), hidden, inter, s))
+        _lib.check(_lib.lib().swb_ffn_ex(int(gate_config), int(down_config), wg.data_ptr(), wu.data_ptr(),
+                                         wd.data_ptr(), x.data_ptr(), _ptr(bg), _ptr(bu), _ptr(bd), h.data_ptr(),
+                                         y.data_ptr(), hidden, inter, flags, s))
 
 
 def layer_config_ids() -> list[int]:

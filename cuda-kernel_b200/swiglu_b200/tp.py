@@ -72,13 +72,17 @@ class Exchange:
 
 
 def ffn_tp_fused(ex: Exchange, x: torch.Tensor, s: dict, bd: torch.Tensor | None, h: torch.Tensor,
-                 y: torch.Tensor, gate_config: int, down_config: int, stream: int | None = None) -> None:
-    """One rank's layer with the fused all-reduce; y (fp32 [hidden]) ends identical on every rank."""
+                 y: torch.Tensor, gate_config: int, down_config: int, stream: int | None = None,
+                 prefetch_weights: bool = False) -> None:
+    """One rank's layer with the fused all-reduce; y (fp32 [hidden]) ends identical on every rank.
+
+    ``prefetch_weights``: SWB_PREFETCH_WEIGHTS (see binding.ffn)."""
     shard_rows, hidden = s["wg"].shape
     sp = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
     ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    flags = _lib.SWB_PREFETCH_WEIGHTS if prefetch_weights else 0
     with torch.cuda.device(x.device):
-        _lib.check(_lib.lib().swb_ffn_tp_fused(ex.handle, int(gate_config), int(down_config), s["wg"].data_ptr(),
-                                               s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), ptr(s["bg"]),
-                                               ptr(s["bu"]), ptr(bd), h.data_ptr(), y.data_ptr(), hidden,
-                                               shard_rows, sp))
+        _lib.check(_lib.lib().swb_ffn_tp_fused_ex(ex.handle, int(gate_config), int(down_config),
+                                                  s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                                  x.data_ptr(), ptr(s["bg"]), ptr(s["bu"]), ptr(bd), h.data_ptr(),
+                                                  y.data_ptr(), hidden, shard_rows, flags, sp))

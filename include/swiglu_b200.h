@@ -183,6 +183,23 @@ SWB_API int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, con
                              const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,
                              void* stream);
 
+/* swb_ffn and swb_ffn_tp_fused with launch flags (no counterpart in the reference).
+ * SWB_PREFETCH_WEIGHTS: the gate kernel is launched programmatically as well, so
+ * its stream of Wg/Wu may begin while the kernel before it in the stream is still
+ * running -- in a chain of layers (one CUDA graph per decode step) the previous
+ * layer's down kernel and exchange. The caller promises that no kernel issued
+ * before the call writes this call's Wg or Wu; x, h and the exchange are still
+ * touched only after the previous kernel has completed (griddepcontrol.wait).
+ * Ignored for layer ids (the fused layer kernel). Other bits: SWB_E_INPUT. */
+#define SWB_PREFETCH_WEIGHTS 1u
+SWB_API int swb_ffn_ex(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
+                       const void* x, const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden,
+                       int inter, unsigned flags, void* stream);
+SWB_API int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard,
+                                const void* wu_shard, const void* wd_shard, const void* x, const void* bg_shard,
+                                const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,
+                                unsigned flags, void* stream);
+
 /* swiglu_out, src/torch_extension.cu:7-40: the binding's shape / config / alias guards,
  * then the model-rounding gate into h [inter] and the fp16 down projection into
  * y [hidden] (no bias, no residual -- the residual stays in the transformer layer).

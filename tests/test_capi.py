@@ -126,6 +126,12 @@ def test_ffn_guards():
     assert f(1, 999, FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, FAKE, 8, 8, None) == _lib.SWB_E_CONFIG
     assert f(1, 1, FAKE, FAKE, None, FAKE, None, None, None, FAKE, FAKE, 8, 8, None) == _lib.SWB_E_INPUT
     assert f(1, 1, FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, None, 8, 8, None) == _lib.SWB_E_FLOAT_OUTPUT
+    # launch flags: unknown bits are rejected first, before any CUDA call
+    fx = L().swb_ffn_ex
+    assert fx(1, 1, FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, FAKE, 8, 8, 2, None) == _lib.SWB_E_INPUT
+    assert b"unknown launch flags" in L().swb_last_error()
+    assert fx(1, 999, FAKE, FAKE, FAKE, FAKE, None, None, None, FAKE, FAKE, 8, 8,
+              _lib.SWB_PREFETCH_WEIGHTS, None) == _lib.SWB_E_CONFIG
 
 
 def test_epilogue_guards():
@@ -162,6 +168,10 @@ def test_tp_exchange_guards_without_gpu():
     assert L().swb_tp_destroy(None) == _lib.SWB_OK
     f = L().swb_ffn_tp_fused
     assert f(None, 83, 83, *([FAKE] * 9), 64, 32, None) == _lib.SWB_E_INPUT
+    fx = L().swb_ffn_tp_fused_ex
+    assert fx(None, 83, 83, *([FAKE] * 9), 64, 32, 4, None) == _lib.SWB_E_INPUT
+    assert b"unknown launch flags" in L().swb_last_error()
+    assert fx(None, 83, 83, *([FAKE] * 9), 64, 32, _lib.SWB_PREFETCH_WEIGHTS, None) == _lib.SWB_E_INPUT
 
 
 def test_ctypes_declarations_match_header_arity():

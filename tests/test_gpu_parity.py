@@ -326,6 +326,49 @@ def test_fused_layer_kernel_matches_oracle(shape):
     assert binding.device_error() == 0
 
 
+@pytest.mark.parametrize("gcfg,dcfg", [(69, 87), (33, 35), (82, 82), (96, 87)])
+def test_prefetch_chain_matches_plain_calls(gcfg, dcfg):
+    """Layers chained back to back with SWB_PREFETCH_WEIGHTS (each gate starts streaming its
+    weights while the previous layer's down kernel still runs; x, h touched only after it
+    completes) give bit-identical outputs to plain calls, eagerly and in one CUDA graph."""
+    H, I = 2048, 5632
+    d = [{k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in O.normal_workload(seed, H, I).items()}
+         for seed in (0, 1)]
+    h = torch.empty(I, dtype=torch.float16, device="cuda")
+    ref = []
+    for k in range(2):
+        y = torch.empty(H, dtype=torch.float32, device="cuda")
+        binding.ffn(d[k]["x"], d[k]["wg"], d[k]["wu"], d[k]["wd"], d[k]["bg"], d[k]["bu"], d[k]["bd"], h, y, gcfg, dcfg)
+        torch.cuda.synchronize()
+        ref.append(y.clone())
+    ys = [torch.empty(H, dtype=torch.float32, device="cuda") for _ in range(4)]
+    stream = torch.cuda.Stream()
+
+    def chain():
+        for k in range(4):
+            w = d[k % 2]
+            binding.ffn(w["x"], w["wg"], w["wu"], w["wd"], w["bg"], w["bu"], w["bd"], h, ys[k], gcfg, dcfg,
+                        stream=stream.cuda_stream, prefetch_weights=True)
+
+    with torch.cuda.stream(stream):
+        chain()
+        stream.synchronize()
+        for k in range(4):
+            assert torch.equal(ys[k], ref[k % 2]), k
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            chain()
+        for _ in range(3):
+            for yk in ys:
+                yk.zero_()
+            g.replay()
+            stream.synchronize()
+            for k in range(4):
+                assert torch.equal(ys[k], ref[k % 2]), k
+        g.reset()
+    assert binding.device_error() == 0
+
+
 def test_fused_layer_in_cuda_graph_and_unsupported_shapes():
     case = Case(2048, 5632)
     d = case.d

@@ -156,3 +156,53 @@ def test_fused_tp_single_rank_eager_and_graph_replays():
     with pytest.raises(RuntimeError, match="RBULK"):
         T.ffn_tp_fused(ex, x, s, bd, h, y, 69, 33)
     ex.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gcfg", [69, 33, 82, 96])
+def test_fused_tp_prefetch_chain_matches_plain(gcfg):
+    """A rank's fused layers chained with SWB_PREFETCH_WEIGHTS (each gate starts streaming while
+    the previous layer's down + exchange runs; the epoch advance waits for it) are bit-identical
+    to plain calls, eagerly and in one CUDA graph (one-rank exchange)."""
+    from swiglu_b200 import binding
+    from swiglu_b200 import tp as T
+    H, I, n = 4096, 14336, 8
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    shards, xs = [], []
+    for seed in (0, 1):
+        w = O.normal_workload(seed, H, I)
+        shards.append(T.shard(t(w["wg"]), t(w["wu"]), t(w["wd"]), t(w["bg"]), t(w["bu"]), 3, n))
+        xs.append((t(w["x"]), t(w["bd"])))
+    ex = T.Exchange(0, 1, H, dev)
+    h = torch.empty(I // n, dtype=torch.float16, device=dev)
+    ref = []
+    for k in range(2):
+        y = torch.empty(H, dtype=torch.float32, device=dev)
+        T.ffn_tp_fused(ex, xs[k][0], shards[k], xs[k][1], h, y, gcfg, 87)
+        torch.cuda.synchronize()
+        ref.append(y.clone())
+    ys = [torch.empty(H, dtype=torch.float32, device=dev) for _ in range(6)]
+    stream = torch.cuda.Stream(dev)
+
+    def chain():
+        for k in range(6):
+            T.ffn_tp_fused(ex, xs[k % 2][0], shards[k % 2], xs[k % 2][1], h, ys[k], gcfg, 87,
+                           stream=stream.cuda_stream, prefetch_weights=True)
+
+    with torch.cuda.stream(stream):
+        chain()
+        stream.synchronize()
+        assert all(torch.equal(ys[k], ref[k % 2]) for k in range(6))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            chain()
+        for _ in range(3):
+            for yk in ys:
+                yk.zero_()
+            g.replay()
+            stream.synchronize()
+            assert all(torch.equal(ys[k], ref[k % 2]) for k in range(6))
+        g.reset()
+    assert binding.device_error() == 0
+    ex.close()

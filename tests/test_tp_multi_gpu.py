@@ -79,6 +79,26 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
         T.ffn_tp_fused(ex, x, s, bd, h, yk, gate, down)
     torch.cuda.synchronize()
     out.extend(yk.cpu().numpy().copy() for yk in ys)
+    # layers chained with SWB_PREFETCH_WEIGHTS in one CUDA graph: bit-identical to plain calls
+    plain = torch.empty_like(y)
+    T.ffn_tp_fused(ex, x, s, bd, h, plain, 69, 87)
+    torch.cuda.synchronize()  # calls on one exchange must not overlap (the chain runs on another stream)
+    chain_ys = [torch.empty_like(y) for _ in range(4)]
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for yk in chain_ys:  # warm (and NCCL-free): eager chain first
+            T.ffn_tp_fused(ex, x, s, bd, h, yk, 69, 87, stream=stream.cuda_stream, prefetch_weights=True)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for yk in chain_ys:
+                T.ffn_tp_fused(ex, x, s, bd, h, yk, 69, 87, stream=stream.cuda_stream, prefetch_weights=True)
+        for yk in chain_ys:
+            yk.zero_()
+        g.replay()
+        stream.synchronize()
+        g.reset()
+    torch.cuda.synchronize()
+    assert all(torch.equal(yk, plain) for yk in chain_ys)
     dist.barrier()
     assert binding.device_error() == 0
     ex.close()
