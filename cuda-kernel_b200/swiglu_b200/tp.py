@@ -34,11 +34,29 @@ def shard(wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, bg, bu, rank: in
     return out
 
 
+def share_handles(mine: bytes, world: int, group=None) -> list[bytes]:
+    """Every rank's exchange IPC handle, in rank order (one all_gather over the process group).
+
+    A rank that never joins makes the others' call fail with the process group's timeout
+    instead of hanging; a malformed handle from any rank raises ValueError on every rank
+    (all of them see the same gathered list)."""
+    import torch.distributed as dist
+    if len(mine) != _lib.SWB_TP_HANDLE_BYTES:
+        raise ValueError(f"exchange handle must be {_lib.SWB_TP_HANDLE_BYTES} bytes, got {len(mine)}")
+    if world == 1:
+        return [bytes(mine)]
+    gathered = [None] * world
+    dist.all_gather_object(gathered, bytes(mine), group=group)
+    bad = [r for r, h in enumerate(gathered) if not isinstance(h, bytes) or len(h) != _lib.SWB_TP_HANDLE_BYTES]
+    if bad:
+        raise ValueError(f"malformed exchange handle from rank(s) {bad}")
+    return gathered
+
+
 class Exchange:
     """This rank's fused-all-reduce exchange buffer, mapped into every rank."""
 
     def __init__(self, rank: int, world: int, rows: int, device: torch.device, group=None):
-        import torch.distributed as dist
         self.rank, self.world, self.rows, self.device = rank, world, rows, device
         L = _lib.lib()
         self._ptr = ctypes.c_void_p()
@@ -46,11 +64,7 @@ class Exchange:
             _lib.check(L.swb_tp_create(rank, world, rows, ctypes.byref(self._ptr)))
             mine = (ctypes.c_uint8 * _lib.SWB_TP_HANDLE_BYTES)()
             _lib.check(L.swb_tp_ipc_handle(self._ptr, mine))
-            if world > 1:
-                gathered = [None] * world
-                dist.all_gather_object(gathered, bytes(mine), group=group)
-            else:
-                gathered = [bytes(mine)]
+            gathered = share_handles(bytes(mine), world, group)
             table = (ctypes.c_uint8 * (_lib.SWB_TP_HANDLE_BYTES * world)).from_buffer_copy(b"".join(gathered))
             _lib.check(L.swb_tp_connect(self._ptr, table))
 

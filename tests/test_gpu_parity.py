@@ -369,6 +369,63 @@ def test_prefetch_chain_matches_plain_calls(gcfg, dcfg):
     assert binding.device_error() == 0
 
 
+PAD = 256
+SENTINEL = {torch.float16: -1234.0, torch.float32: -98765.0}
+
+
+def guarded(n, dtype):
+    """A length-n output inside a buffer whose PAD elements on each side hold a sentinel."""
+    buf = torch.full((n + 2 * PAD,), SENTINEL[dtype], dtype=dtype, device="cuda")
+    return buf, buf[PAD:PAD + n]
+
+
+def pads_intact(buf):
+    s = SENTINEL[buf.dtype]
+    return bool(torch.all(buf[:PAD] == s).item()) and bool(torch.all(buf[-PAD:] == s).item())
+
+
+@pytest.mark.parametrize("shape", [(17, 33), (37, 65), (2047, 5631), (4096, 1792)])
+def test_outputs_stay_in_their_bounds(shape, ids):
+    """Guard-band canaries: every geometry writes exactly its output elements (gate h, fp32
+    and fp16 projections, the layer, the fused single-rank exchange, the fused layer kernel),
+    at odd sizes and tensor-parallel shard sizes; the sentinel pads either side survive."""
+    from swiglu_b200 import tp as T
+    H, I = shape
+    g = torch.Generator(device="cuda").manual_seed(5)
+    r = lambda *sz: (torch.randn(*sz, generator=g, device="cuda") * 0.05).half()  # noqa: E731
+    wg, wu, wd, x, bg, bu, bd = r(I, H), r(I, H), r(H, I), r(H), r(I), r(I), r(H)
+    for cfg in ids:
+        hb, h = guarded(I, torch.float16)
+        binding.gate(wg, wu, x, h, cfg, bg, bu)
+        yb, y = guarded(H, torch.float32)
+        binding.project(wd, h, y, cfg, bias=bd, residual=x)
+        yhb, yh = guarded(H, torch.float16)
+        binding.project(wd, h, yh, cfg)
+        hb2, h2 = guarded(I, torch.float16)
+        yb2, y2 = guarded(H, torch.float32)
+        binding.ffn(x, wg, wu, wd, bg, bu, bd, h2, y2, cfg, cfg)
+        torch.cuda.synchronize()
+        assert all(pads_intact(b) for b in (hb, yb, yhb, hb2, yb2)), cfg
+    if H % 8 == 0 and I % 8 == 0:
+        ex = T.Exchange(0, 1, H, torch.device("cuda", 0))
+        s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
+        for gate_cfg, down_cfg in ((69, 87), (33, 83), (82, 80)) + tuple((lid, 0) for lid in binding.layer_config_ids()):
+            hb, h = guarded(I, torch.float16)
+            yb, y = guarded(H, torch.float32)
+            T.ffn_tp_fused(ex, x, s, bd, h, y, gate_cfg, down_cfg)
+            torch.cuda.synchronize()
+            assert pads_intact(hb) and pads_intact(yb), (gate_cfg, down_cfg)
+        ex.close()
+        ws = binding.layer_workspace()
+        for lid in binding.layer_config_ids():
+            hb, h = guarded(I, torch.float16)
+            yb, y = guarded(H, torch.float32)
+            binding.ffn_fused(x, wg, wu, wd, bg, bu, bd, h, y, lid, ws)
+            torch.cuda.synchronize()
+            assert pads_intact(hb) and pads_intact(yb), lid
+    assert binding.device_error() == 0
+
+
 def test_fused_layer_in_cuda_graph_and_unsupported_shapes():
     case = Case(2048, 5632)
     d = case.d

@@ -206,3 +206,144 @@ def test_fused_tp_prefetch_chain_matches_plain(gcfg):
         g.reset()
     assert binding.device_error() == 0
     ex.close()
+
+
+def _handles_worker(rank, world, port, mode, q):
+    import datetime
+    import time
+    import torch.distributed as dist
+    from swiglu_b200 import tp as T
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    mine = bytes([rank + 1]) * 64
+    t0 = time.monotonic()
+    try:
+        if rank == 1 and mode == "absent":
+            q.put((rank, "left", 0.0))
+            q.close()
+            q.join_thread()  # the message is out before the process vanishes
+            os._exit(0)  # leaves without joining the exchange (and without shutting the group down)
+        if rank == 1 and mode == "malformed":
+            dist.all_gather_object([None] * world, b"short")  # bypasses its own check
+            q.put((rank, "sent", 0.0))
+            return
+        handles = T.share_handles(mine, world)
+        q.put((rank, [h[0] for h in handles], time.monotonic() - t0))
+    except Exception as exc:  # noqa: BLE001 -- reported to the parent
+        q.put((rank, f"{type(exc).__name__}: {exc}"[:200], time.monotonic() - t0))
+    finally:
+        if not (rank == 1 and mode == "absent"):
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                pass
+
+
+@pytest.mark.parametrize("mode", ["ok", "absent", "malformed"])
+def test_exchange_handle_sharing_fails_cleanly_gloo(mode):
+    """Set-up of the fused exchange on CPU ranks: every rank gets every handle in rank order;
+    a rank that never joins makes the other's set-up raise within the group's timeout (no
+    hang); a malformed handle raises on the rank that receives it."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_handles_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, out, dt = q.get(timeout=120)
+        got[rank] = (out, dt)
+    for p in procs:
+        p.join(timeout=60)
+    if mode == "ok":
+        assert got[0][0] == [1, 2] and got[1][0] == [1, 2]
+    elif mode == "absent":
+        assert got[1][0] == "left"
+        assert isinstance(got[0][0], str) and got[0][1] < 60  # an error, within the timeout scale
+    else:
+        assert isinstance(got[0][0], str) and got[0][0].startswith("ValueError")
+
+
+def _idle_peer_proc(role, H, hq, tq, rq, done):
+    """One rank of a two-rank exchange on GPU 0 (see test_peer_wait_times_out_and_reports)."""
+    import ctypes
+    import sys
+    import time
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "cuda-kernel_b200")]
+    import torch
+    from swiglu_b200 import _lib, binding
+    torch.cuda.set_device(0)
+    L = _lib.lib()
+    tp = ctypes.c_void_p()
+    _lib.check(L.swb_tp_create(role, 2, H, ctypes.byref(tp)))
+    mine = (ctypes.c_uint8 * _lib.SWB_TP_HANDLE_BYTES)()
+    _lib.check(L.swb_tp_ipc_handle(tp, mine))
+    hq.put((role, bytes(mine)))
+    table = tq.get(timeout=120)
+    buf = (ctypes.c_uint8 * len(table)).from_buffer_copy(table)
+    _lib.check(L.swb_tp_connect(tp, buf))
+    if role == 1:
+        # holds its buffer mapped and never calls: nothing writes rank 1's slots in rank 0's buffer
+        rq.put((1, "ready", 0.0))
+        done.wait(120)
+        L.swb_tp_destroy(tp)
+        return
+    I = 256
+    dev = torch.device("cuda", 0)
+    wg = (torch.randn(I, H, device=dev) * 0.05).half()
+    wu = (torch.randn(I, H, device=dev) * 0.05).half()
+    wd = (torch.randn(H, I, device=dev) * 0.05).half()
+    x = torch.randn(H, device=dev).half()
+    h = torch.empty(I, dtype=torch.float16, device=dev)
+    y = torch.full((H,), 7.0, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    binding.device_error(clear=True)
+    t0 = time.monotonic()
+    _lib.check(L.swb_ffn_tp_fused(tp, 69, 87, wg.data_ptr(), wu.data_ptr(), wd.data_ptr(), x.data_ptr(), None, None,
+                                  None, h.data_ptr(), y.data_ptr(), H, I, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    elapsed = time.monotonic() - t0
+    err = binding.device_error(clear=True)
+    untouched = bool(torch.all(y == 7.0).item())  # rows whose peer did not deliver are not written
+    usable = float(torch.ones(8, device=dev).sum().item()) == 8.0
+    L.swb_tp_destroy(tp)
+    rq.put((0, (err, elapsed, untouched, usable), elapsed))
+    done.set()
+
+
+@pytest.mark.gpu
+def test_peer_wait_times_out_and_reports():
+    """Failure detection without a GPU fault: rank 1 of a two-rank exchange (a second process
+    on the same GPU) maps its buffer but never runs the layer -- a flag nothing sets. Rank 0's
+    fused layer stores its partials, waits (bounded, 1 s) for rank 1's, gives up, returns
+    without writing y and reports SWB_DEVERR_PEER_TIMEOUT; the context stays usable. Only one
+    kernel ever waits, and every store lands in memory that stays mapped."""
+    import torch.multiprocessing as mp
+    H = 512
+    ctx = mp.get_context("spawn")
+    hq, rq = ctx.Queue(), ctx.Queue()
+    tqs = [ctx.Queue(), ctx.Queue()]
+    done = ctx.Event()
+    procs = [ctx.Process(target=_idle_peer_proc, args=(r, H, hq, tqs[r], rq, done)) for r in range(2)]
+    for p in procs:
+        p.start()
+    handles = dict(hq.get(timeout=180) for _ in range(2))
+    table = handles[0] + handles[1]
+    for q in tqs:
+        q.put(table)
+    results = {}
+    for _ in range(2):
+        rank, out, _ = rq.get(timeout=180)
+        results[rank] = out
+    done.set()
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    err, elapsed, untouched, usable = results[0]
+    assert err & 2, err  # SWB_DEVERR_PEER_TIMEOUT
+    assert 0.9 < elapsed < 30, elapsed
+    assert untouched and usable
