@@ -221,7 +221,7 @@ def main():
     p.add_argument("--layers", type=int, default=22)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-tune", action="store_true")
-    p.add_argument("--output", type=Path, default=Path("gpurun_out/model.json"))
+    p.add_argument("--output", type=Path, default=Path("results/model.json"))
     a = p.parse_args()
     if not 1 <= a.tokens <= 256 or not 3 <= a.samples <= 31:
         raise SystemExit("tokens must be 1..256 and samples 3..31")

@@ -79,7 +79,7 @@ def write_json(path: Path, data) -> None:
 
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__)
-    p.add_argument("--output-dir", type=Path, default=Path("gpurun_out/results"))
+    p.add_argument("--output-dir", type=Path, default=Path("results"))
     p.add_argument("--probe-only", action="store_true")
     p.add_argument("--model", action="store_true")
     p.add_argument("--skip-build", action="store_true")

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parents[1]
 
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__)
-    p.add_argument("--output", type=Path, default=Path("gpurun_out/sweep"))
+    p.add_argument("--output", type=Path, default=Path("results/sweep"))
     p.add_argument("--seeds", default="17,101,997")
     p.add_argument("--suites", default="correctness,decode")
     p.add_argument("--model", action="store_true")
