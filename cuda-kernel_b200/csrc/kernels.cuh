@@ -9,15 +9,21 @@
 //   MODE_F16 : the same rounded to fp16.
 // These replace decode::project (include/kernels.cuh:24-114 of shubhxho/cuda-kernel).
 //
-// Two families:
-//   ldg_kernel  -- rows spread over CTAs, 128-bit (or 32-bit) streaming loads
-//                  with UNROLL loads per matrix in flight per thread, x staged
-//                  once per CTA in shared memory as fp32;
-//   bulk_kernel -- persistent: each CTA owns a balanced contiguous row range and
-//                  a producer thread streams it with cp.async.bulk into a ring
-//                  of shared-memory stages guarded by mbarriers; consumer warps
-//                  read each stage once. Row partial sums are combined in a
-//                  fixed order, so every configuration is deterministic.
+// Families (one registry, csrc/registry.h):
+//   ldg_kernel   -- rows spread over CTAs, 128-bit (or 32-bit) streaming loads
+//                   with UNROLL loads per matrix in flight per thread, x staged
+//                   once per CTA in shared memory as fp32;
+//   bulk_kernel  -- persistent: each CTA owns a balanced contiguous row range and
+//                   a producer thread streams it with cp.async.bulk into a ring
+//                   of shared-memory stages guarded by mbarriers; consumer warps
+//                   read each stage once;
+//   rbulk_kernel -- as bulk_kernel, but a stage holds whole rows and each
+//                   consumer thread keeps its slice of x in registers;
+//                   rbulk_allreduce_kernel adds the tensor-parallel exchange;
+//   sbulk_kernel -- rbulk's stages with hardware work stealing (cluster launch
+//                   control) over row blocks.
+// Row partial sums are combined in a fixed order, so every configuration is
+// deterministic. Every wait is bounded (device.cuh).
 #pragma once
 
 #include <type_traits>

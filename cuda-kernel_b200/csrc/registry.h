@@ -21,7 +21,8 @@
 //   unroll = MAXJ, the 16-byte vectors of a row each consumer thread owns
 //            (so cols <= 8 * 32 * warps * unroll),
 //   chunk  = target bytes per ring stage (whole rows, at least one),
-//   stages = maximum ring depth (trimmed to the shared memory available).
+//   stages = maximum ring depth (trimmed to the shared memory available and
+//            to the CTA's stages of work).
 //   An RBULK id whose preconditions fail runs the BULK geometry of id 64.
 // SBULK family (RBULK with hardware work stealing): same fields as RBULK; the
 //   grid has one CTA per small block of rows and running CTAs take over blocks

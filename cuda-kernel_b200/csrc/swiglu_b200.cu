@@ -117,9 +117,11 @@ int ensure_smem(Kernel kernel, std::atomic<uint64_t>& done_mask, size_t bytes) {
 }
 
 // Launches `kernel`; with `pdl` the launch may begin before the previous kernel
-// in the stream finishes (programmatic dependent launch). Only used for the
-// down projection right after this library's own gate kernel: the down kernel
-// reads nothing the gate writes until its griddepcontrol.wait.
+// in the stream finishes (programmatic dependent launch). Used for the down
+// projection right after this library's own gate kernel (the down kernel reads
+// nothing the gate writes until its griddepcontrol.wait), and for the gate under
+// SWB_PREFETCH_WEIGHTS (only its weight stream starts early; x, h and the
+// exchange epoch wait for griddepcontrol.wait).
 template <typename Kernel>
 void launch_kernel(Kernel kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t stream, bool pdl,
                    const Params& p) {
