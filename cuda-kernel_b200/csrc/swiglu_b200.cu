@@ -825,7 +825,7 @@ int swb_tp_connect(swb_tp_t* tp, const void* handles) {
     if (!tp || !handles) return fail(SWB_E_INPUT, "null exchange or handles");
     if (tp->connected) return SWB_OK;
     for (int q = 0; q < tp->world; ++q) {
-        if (q == tp->rank) continue;
+        if (q == tp->rank || tp->peer[q]) continue;  // a retry after a partial failure keeps what it opened
         cudaIpcMemHandle_t h;
         std::memcpy(&h, static_cast<const char*>(handles) + size_t(q) * SWB_TP_HANDLE_BYTES, sizeof h);
         void* p = nullptr;
@@ -859,6 +859,9 @@ int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const vo
                         void* stream) {
     if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
     if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != tp->device)
+        return fail(SWB_E_INPUT, "the current device is not the exchange's device");
     if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
     const bool layer = is_layer_config(gate_config);
     if (!layer && (!find_config(gate_config) || !find_config(down_config))) return fail(SWB_E_CONFIG);
