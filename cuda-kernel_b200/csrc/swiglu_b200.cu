@@ -920,6 +920,7 @@ int swb_ffn_fused(int layer_config, const void* wg, const void* wu, const void* 
     if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
     if (!y) return fail(SWB_E_FLOAT_OUTPUT);
     if (!workspace) return fail(SWB_E_WORKSPACE, "swb_ffn_fused needs its SWB_LAYER_WORKSPACE_BYTES workspace");
+    if (reinterpret_cast<uintptr_t>(workspace) % 16) return fail(SWB_E_WORKSPACE, "workspace must be 16-byte aligned");
     LayerParams L;
     std::memset(&L, 0, sizeof L);
     L.wg = static_cast<const __half*>(wg);

@@ -42,7 +42,8 @@ extern "C" {
 #define SWB_E_CUDA 12          /* CUDA runtime error; detail in swb_last_error() */
 #define SWB_E_DEVICE 13        /* a kernel gave up a bounded wait (device error word set) */
 #define SWB_E_UNSUPPORTED 14   /* no usable sm_100 device / feature */
-#define SWB_E_WORKSPACE 15     /* size beyond the built-in workspace of swb_ffn_noalloc */
+#define SWB_E_WORKSPACE 15     /* size beyond the built-in workspace of swb_ffn_noalloc; a missing
+                                  or misaligned swb_ffn_fused workspace */
 
 /* project() flags (template flags of decode::launch, include/kernels.cuh:136) */
 #define SWB_RESIDUAL 1u /* add residual[row] after bias (RESIDUAL) */
@@ -127,7 +128,7 @@ SWB_API int swb_ffn_noalloc(int gate_config, int down_config, const void* wg, co
 /* The whole layer in ONE persistent kernel (no counterpart in the reference): gate
  * rows, a grid barrier, then down rows, with the weight stream running straight
  * from Wg/Wu into Wd. Same arguments and outputs as swb_ffn plus `workspace`:
- * SWB_LAYER_WORKSPACE_BYTES of device memory, zeroed once when allocated, then
+ * SWB_LAYER_WORKSPACE_BYTES of 16-byte aligned device memory, zeroed once when allocated, then
  * reused by every call on one stream (calls sharing a workspace must not overlap).
  * layer_config is a layer id (swb_layer_config_ids); a geometry that cannot hold
  * a row of the shape falls back to 200, then 203. Needs hidden and inter

@@ -192,5 +192,7 @@ def test_layer_registry_and_fused_guards():
     f = L().swb_ffn_fused
     assert f(33, *([FAKE] * 9), 64, 96, FAKE, None) == _lib.SWB_E_CONFIG        # projection id, not a layer id
     assert f(200, *([FAKE] * 9), 64, 96, None, None) == _lib.SWB_E_WORKSPACE
+    assert f(200, *([FAKE] * 9), 64, 96, ctypes.c_void_p(0x1004), None) == _lib.SWB_E_WORKSPACE  # misaligned
+    assert b"16-byte aligned" in L().swb_last_error()
     assert f(200, None, *([FAKE] * 8), 64, 96, FAKE, None) == _lib.SWB_E_INPUT
     assert f(200, FAKE, None, *([FAKE] * 7), 64, 96, FAKE, None) == _lib.SWB_E_GATE_BUFFERS
