@@ -58,6 +58,8 @@ def parse():
                    help="launch each step's gate in plain stream order (no SWB_PREFETCH_WEIGHTS)")
     p.add_argument("--layer-config", type=int, default=0,
                    help="fused whole-layer kernel id (0 = tune against the two-kernel path, -1 = never)")
+    p.add_argument("--fixture", type=Path, default=None,
+                   help="captured layer directory (swiglu_b200.fixtures) of --hidden x --intermediate")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-cublas", action="store_true")
@@ -234,6 +236,14 @@ def ours(args) -> None:
 
     # Full weights are drawn on every rank from the same seed, then each rank keeps its shard.
     full_sets, common = make_weights(torch, H, I, copies, device)
+    if args.fixture is not None:
+        # a captured layer (src/benchmark.cu:122-127): every rotating copy holds its weights
+        from swiglu_b200.fixtures import as_layer, load
+        cap = {k: torch.from_numpy(v.copy()).to(device) for k, v in as_layer(load(args.fixture, H, I)).items()}
+        for s in full_sets:
+            for k in ("wg", "wu", "wd"):
+                s[k].copy_(cap[k])
+        common = {"x": cap["x"], "bg": cap["bg"], "bu": cap["bu"], "bd": cap["bd"]}
     r0, r1 = rank * shard, (rank + 1) * shard
     sets = []
     for s in full_sets:
@@ -659,7 +669,8 @@ def ours(args) -> None:
             "metric": METRIC, "value": us_per_layer, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "one_step_graph_us": one_step_us,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+            "data": "captured-model-fixture" if args.fixture is not None else "synthetic",
             "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
                        "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
                        "layer_config": lcfg or None,
@@ -669,7 +680,12 @@ def ours(args) -> None:
                        "rotating_copies": copies,
                        "l2": f"inputs larger than L2: {copies} rotating weight copies of "
                              f"{weight_bytes_rank / 2**20:.0f} MiB per rank",
-                       "seed": 0, "weights": "N(0, 1/sqrt(K)) fp16", "x": "N(0,1)", "bias": "N(0,0.02)"},
+                       "seed": 0, "weights": "N(0, 1/sqrt(K)) fp16", "x": "N(0,1)", "bias": "N(0,0.02)"}
+                      if args.fixture is None else
+                      {"workload": f"SwiGLU FFN {H}->{I} batch 1 (captured layer)", "hidden": H, "intermediate": I,
+                       "batch": 1, "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
+                       "layer_config": lcfg or None, "prefetch_weights": bool(flags),
+                       "rotating_copies": copies, "fixture": str(args.fixture)},
             "roofline": roofline, "layer_roofline": layer_roofline, "cpu_baseline": cpu, "e2e": e2e,
             "cublas_baseline": cublas, "tp": tp, "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
             "gpu_name": torch.cuda.get_device_name(device),

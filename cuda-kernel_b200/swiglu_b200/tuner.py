@@ -51,9 +51,12 @@ def shapes(suite: str):
 
 
 class Workload:
-    """Seeded inputs on the GPU, rotating weight copies, float64 references."""
+    """Seeded inputs on the GPU, rotating weight copies, float64 references.
 
-    def __init__(self, torch, hidden, inter, seed, dist, device):
+    With ``fixture`` (arrays of swiglu_b200.fixtures.load) every copy holds the captured
+    layer and x and the biases are the captured ones (src/benchmark.cu:122-127)."""
+
+    def __init__(self, torch, hidden, inter, seed, dist, device, fixture=None):
         self.torch, self.hidden, self.inter, self.device = torch, hidden, inter, device
         g = torch.Generator(device=device).manual_seed(seed)
         f16 = torch.float16
@@ -77,6 +80,13 @@ class Workload:
         self.bg = draw((inter,), 0.1 if uni else 0.02)
         self.bu = draw((inter,), 0.1 if uni else 0.02)
         self.bd = draw((hidden,), 0.1 if uni else 0.02)
+        if fixture is not None:
+            from .fixtures import as_layer
+            f = {k: torch.from_numpy(v.copy()).to(device) for k, v in as_layer(fixture).items()}
+            for s in self.sets:
+                for k in ("wg", "wu", "wd"):
+                    s[k].copy_(f[k])
+            self.x, self.bg, self.bu, self.bd = f["x"], f["bg"], f["bu"], f["bd"]
         self.h = torch.empty(inter, dtype=f16, device=device)
         self.g = torch.empty(inter, dtype=torch.float32, device=device)
         self.u = torch.empty(inter, dtype=torch.float32, device=device)
@@ -294,13 +304,23 @@ def run_case(torch, L, base, w, name, ffn, ids, repeats, samples, transfers, str
 
 
 def run(suite="decode", repeats=100, samples=9, seed=17, dist="normal", include_transfers=False,
-        ids=None, device_index=0) -> dict:
+        ids=None, device_index=0, fixture=None, hidden=0, intermediate=0) -> dict:
     import torch
     from . import _lib, intensity
     from .binding import CublasBaseline, config_ids, cuda_versions
 
     if not 3 <= samples <= 101 or not 1 <= repeats <= 10000:
         raise ValueError("samples must be 3..101 and repeats 1..10000")
+    cases = shapes(suite)
+    captured = None
+    if fixture:  # src/benchmark.cu:319-322
+        if not hidden or not intermediate:
+            raise ValueError("fixture needs --hidden and --intermediate")
+        from .fixtures import load
+        captured = load(fixture, hidden, intermediate)
+        cases = [("captured-model-ffn", hidden, intermediate)]
+    elif hidden or intermediate:
+        raise ValueError("custom dimensions require --fixture")
     device = torch.device("cuda", device_index)
     torch.cuda.set_device(device)
     stream = torch.cuda.Stream(device)
@@ -318,10 +338,11 @@ def run(suite="decode", repeats=100, samples=9, seed=17, dist="normal", include_
               "suite": suite, "seed": seed, "repeats": repeats, "samples": samples, "timing": "cuda-graph-events",
               "cache_policy": "rotating-weight-copies-over-2x-L2",
               "transfer_timing": "h2d-input-kernel-d2h-output-events" if include_transfers else "omitted",
-              "data": "synthetic-fp16-model-shapes", "distribution": dist, "atol": ATOL, "rtol": RTOL,
+              "data": "captured-model-fixture" if captured is not None else "synthetic-fp16-model-shapes",
+              "distribution": dist, "atol": ATOL, "rtol": RTOL,
               "hbm_peak_gbs": peaks["hbm_gbs"], "hbm_peak_source": peaks["source"], "cases": []}
-    for name, hidden, inter in shapes(suite):
-        w = Workload(torch, hidden, inter, seed, dist, device)
+    for name, hidden, inter in cases:
+        w = Workload(torch, hidden, inter, seed, dist, device, fixture=captured)
         for ffn in (False, True):
             result["cases"].append(run_case(torch, L, base, w, name, ffn, ids, repeats, samples,
                                             include_transfers, stream))
@@ -341,9 +362,13 @@ def main(argv=None):
     p.add_argument("--include-transfers", action="store_true")
     p.add_argument("--configs", type=str, default="", help="comma-separated registry ids (default: all)")
     p.add_argument("--output", type=Path)
+    p.add_argument("--fixture", type=Path, help="captured layer directory (swiglu_b200.fixtures)")
+    p.add_argument("--hidden", type=int, default=0)
+    p.add_argument("--intermediate", type=int, default=0)
     a = p.parse_args(argv)
     ids = [int(v) for v in a.configs.split(",") if v] or None
-    result = run(a.suite, a.repeats, a.samples, a.seed, a.dist, a.include_transfers, ids)
+    result = run(a.suite, a.repeats, a.samples, a.seed, a.dist, a.include_transfers, ids,
+                 fixture=a.fixture, hidden=a.hidden, intermediate=a.intermediate)
     from . import report
     report.validate(result)
     text = json.dumps(result) + "\n"
