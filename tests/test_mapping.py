@@ -459,3 +459,99 @@ def test_layer_kernel_plans_cover_both_phases():
                         assert nm * ru * cols * 2 < (1 << 20)
                         owner[row:row + ru] += 1
                 assert (owner == 1).all()
+
+
+# ------------------------------------------------- grouped rows (stage_rows)
+
+def reduce_scatter(values, K):
+    """warp_reduce_scatter<K> (csrc/kernels.cuh) on 32 lanes x K float32 values: lane -> total."""
+    v = [[np.float32(x) for x in values[lane]] for lane in range(32)]
+    k, d = K, 16
+    while k > 1:
+        nxt = []
+        for lane in range(32):
+            p = lane ^ d
+            upper, p_upper = bool(lane & d), bool(p & d)
+            row = list(v[lane])
+            for i in range(k // 2):
+                keep = v[lane][i + k // 2] if upper else v[lane][i]
+                recv = v[p][i] if p_upper else v[p][i + k // 2]  # what the partner sends
+                row[i] = np.float32(keep + recv)
+            nxt.append(row)
+        v, k, d = nxt, k // 2, d // 2
+    lk = int(math.log2(K))
+    t = [v[lane][0] for lane in range(32)]
+    d = 16 >> lk
+    while d:
+        t = [np.float32(t[lane] + t[lane ^ d]) for lane in range(32)]
+        d //= 2
+    return t
+
+
+@pytest.mark.parametrize("nm", [1, 2])
+@pytest.mark.parametrize("rg", [1, 2, 4, 8])
+def test_stage_rows_group_reduction_and_writers(rg, nm):
+    """Each row of a group is summed over all 32 lanes and stored exactly once, by the lane
+    holding it (lane & (32/K - 1) == 0, value index lane >> (5 - log2 K)), and rows past the
+    stage's end are not stored."""
+    K = rg * nm
+    if K > 8:
+        pytest.skip("not instantiated")
+    rng = np.random.default_rng(K)
+    vals = rng.standard_normal((32, K)).astype(np.float32)
+    totals = reduce_scatter(vals, K)
+    lk = int(math.log2(K))
+    for ru in range(1, rg + 1):  # rows present in the group
+        written = {}
+        for lane in range(32):
+            if lane & ((32 >> lk) - 1):
+                continue
+            idx = lane >> (5 - lk)
+            g, m = idx // nm, idx % nm
+            if g < ru:
+                assert (g, m) not in written
+                written[(g, m)] = totals[lane]
+        assert set(written) == {(g, m) for g in range(ru) for m in range(nm)}
+        for (g, m), t in written.items():
+            assert abs(t - vals[:, g * nm + m].astype(np.float64).sum()) < 1e-4
+
+
+# ----------------------------------------------- tensor-parallel exchange slots
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("hidden,cps", [(4096, 2), (4096, 1), (2048, 2), (520, 2)])
+def test_exchange_slot_map(world, hidden, cps):
+    """tp_exchange_rows (csrc/kernels.cuh): every store lands inside the receiving rank's
+    2 x world x rows slots; in one call each slot a reader waits on is written by exactly one
+    CTA of exactly one peer (the same CTA index: every rank runs the same grid), never twice;
+    a rank never reads its own slot (it keeps its partial in registers); and the two
+    parities of consecutive calls never share a slot."""
+    G = min(SMS * cps, hidden)
+    n_slots = 2 * world * hidden
+    for epoch in (1, 2):
+        par = epoch & 1
+        writes = np.zeros((world, n_slots), np.int64)   # [receiving rank][slot]
+        writer_cta = -np.ones((world, n_slots), np.int64)
+        for src in range(world):
+            for b in range(G):
+                r0, r1 = b * hidden // G, (b + 1) * hidden // G
+                for q in range(world):
+                    if q == src:
+                        continue
+                    idx = (par * world + src) * hidden + np.arange(r0, r1)
+                    assert idx.min(initial=0) >= 0 and idx.max(initial=0) < n_slots
+                    writes[q, idx] += 1
+                    writer_cta[q, idx] = b
+        for me in range(world):
+            for b in range(G):
+                r0, r1 = b * hidden // G, (b + 1) * hidden // G
+                for q in range(world):
+                    if q == me:
+                        continue
+                    idx = par * world * hidden + q * hidden + np.arange(r0, r1)  # mine + q*rows + r0 + i
+                    assert (writes[me, idx] == 1).all() and (writer_cta[me, idx] == b).all()
+            own = par * world * hidden + me * hidden + np.arange(hidden)
+            assert (writes[me, own] == 0).all()
+        assert writes.max(initial=0) <= 1
+        other = (1 - par) * world * hidden + np.arange(world * hidden)
+        assert (writes[:, other] == 0).all()
