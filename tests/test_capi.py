@@ -196,3 +196,53 @@ def test_layer_registry_and_fused_guards():
     assert b"16-byte aligned" in L().swb_last_error()
     assert f(200, None, *([FAKE] * 8), 64, 96, FAKE, None) == _lib.SWB_E_INPUT
     assert f(200, FAKE, None, *([FAKE] * 7), 64, 96, FAKE, None) == _lib.SWB_E_GATE_BUFFERS
+
+
+C_CALLER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "swiglu_b200.h"
+
+#define EXPECT(cond) do { if (!(cond)) { printf("FAIL line %d\n", __LINE__); return 1; } } while (0)
+
+int main(void) {
+    /* the registry, as decode_bench would iterate it */
+    int n = swb_config_count();
+    EXPECT(n > 10);
+    int ids[256];
+    EXPECT(swb_config_ids(ids, 256) == n);
+    EXPECT(ids[0] == 1 && swb_valid_config(1) && !swb_valid_config(0) && !swb_valid_config(999));
+    swb_config_t c;
+    EXPECT(swb_config_info(17, &c) == SWB_OK && c.id == 17 && c.warps == 2 && c.rows == 4 && c.pack == 8);
+    /* guards run before any CUDA call: no GPU is needed for these */
+    void* fake = (void*)0x7f0000000000ull;
+    float* yf = (float*)fake;
+    EXPECT(swb_ffn(1, 999, fake, fake, fake, fake, NULL, NULL, NULL, fake, yf, 8, 8, NULL) == SWB_E_CONFIG);
+    EXPECT(strcmp(swb_status_string(SWB_E_CONFIG), "unknown kernel configuration") == 0);
+    EXPECT(swb_ffn_ex(1, 1, fake, fake, fake, fake, NULL, NULL, NULL, fake, yf, 8, 8, 2u, NULL) == SWB_E_INPUT);
+    EXPECT(strstr(swb_last_error(), "unknown launch flags") != NULL);
+    EXPECT(swb_swiglu_out(fake, fake, fake, fake, fake, fake, 8, 8, 1001, 1, NULL) == SWB_E_CONFIG_RANGE);
+    swb_tp_t* tp = NULL;
+    EXPECT(swb_tp_create(0, 9, 16, &tp) == SWB_E_INPUT && tp == NULL);
+    EXPECT(swb_tp_destroy(NULL) == SWB_OK);
+    puts("C caller ok");
+    return 0;
+}
+"""
+
+
+def test_header_is_plain_c_and_the_library_links(tmp_path):
+    """A C11 caller with no Python and no C++ compiles against the header, links the library
+    and gets the registry and the guards' codes and messages."""
+    import shutil
+    import subprocess
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    src = tmp_path / "caller.c"
+    src.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    libdir = _lib.LIB_PATH.parent
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", f"-I{_lib.REPO_ROOT / 'include'}", str(src),
+                    f"-L{libdir}", "-lswiglu_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0 and "C caller ok" in out.stdout, out.stdout + out.stderr
