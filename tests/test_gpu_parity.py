@@ -21,7 +21,7 @@ import pytest
 import torch
 
 import oracle as O
-from swiglu_b200 import _lib, binding
+from swiglu_b200 import binding
 from swiglu_b200.binding import config_ids
 
 pytestmark = pytest.mark.gpu
