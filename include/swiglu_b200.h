@@ -3,11 +3,13 @@
  *
  *   gate = Wg x + bg,  up = Wu x + bu,  h = SiLU(gate) * up,  y = Wd h + bd + x
  *
- * fp16 weights/inputs, fp32 accumulation, fp16 h, fp32 (or fp16) y. Every entry
- * point takes plain device pointers and sizes, launches asynchronously on the
- * given stream (a cudaStream_t, NULL = legacy default stream) on the CURRENT
- * device, allocates nothing, and returns 0 or a SWB_E_* status. Argument checks
- * run before any CUDA call, so invalid calls fail without touching a GPU.
+ * fp16 weights/inputs, fp32 accumulation, fp16 h, fp32 (or fp16) y. Every layer
+ * and projection entry point takes plain device pointers and sizes, launches
+ * asynchronously on the given stream (a cudaStream_t, NULL = legacy default
+ * stream) on the CURRENT device, allocates nothing, and returns 0 or a SWB_E_*
+ * status; the only allocation is the tensor-parallel exchange buffer, once, in
+ * swb_tp_create. Argument checks run before any CUDA call, so invalid calls fail
+ * without touching a GPU.
  *
  * Each declaration names the interface of shubhxho/cuda-kernel it replaces.
  * Library: cuda-kernel_b200/lib/libswiglu_b200.so (cudart linked statically).
