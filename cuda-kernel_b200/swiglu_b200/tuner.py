@@ -324,32 +324,36 @@ def run(suite="decode", repeats=100, samples=9, seed=17, dist="normal", include_
     device = torch.device("cuda", device_index)
     torch.cuda.set_device(device)
     stream = torch.cuda.Stream(device)
-    torch.cuda.set_stream(stream)
-    L = _lib.lib()
-    base = CublasBaseline(device)
-    ids = ids or config_ids()
-    prop = torch.cuda.get_device_properties(device)
-    driver, runtime = cuda_versions()
-    peaks = intensity.measured_peaks()
-    result = {"schema_version": 1, "result_class": "measured", "gpu": prop.name,
-              "compute_capability": f"{prop.major}.{prop.minor}", "l2_bytes": prop.L2_cache_size,
-              "total_memory_bytes": prop.total_memory, "sm_count": prop.multi_processor_count,
-              "driver_version": driver, "runtime_version": runtime, "cublas_version": base.version(),
-              "suite": suite, "seed": seed, "repeats": repeats, "samples": samples, "timing": "cuda-graph-events",
-              "cache_policy": "rotating-weight-copies-over-2x-L2",
-              "transfer_timing": "h2d-input-kernel-d2h-output-events" if include_transfers else "omitted",
-              "data": "captured-model-fixture" if captured is not None else "synthetic-fp16-model-shapes",
-              "distribution": dist, "atol": ATOL, "rtol": RTOL,
-              "hbm_peak_gbs": peaks["hbm_gbs"], "hbm_peak_source": peaks["source"], "cases": []}
-    for name, hidden, inter in cases:
-        w = Workload(torch, hidden, inter, seed, dist, device, fixture=captured)
-        for ffn in (False, True):
-            result["cases"].append(run_case(torch, L, base, w, name, ffn, ids, repeats, samples,
-                                            include_transfers, stream))
-        del w
-        torch.cuda.empty_cache()
-    base.close()
-    return result
+    prev = torch.cuda.current_stream(device)
+    torch.cuda.set_stream(stream)  # the caller's stream comes back on the way out
+    try:
+        L = _lib.lib()
+        base = CublasBaseline(device)
+        ids = ids or config_ids()
+        prop = torch.cuda.get_device_properties(device)
+        driver, runtime = cuda_versions()
+        peaks = intensity.measured_peaks()
+        result = {"schema_version": 1, "result_class": "measured", "gpu": prop.name,
+                  "compute_capability": f"{prop.major}.{prop.minor}", "l2_bytes": prop.L2_cache_size,
+                  "total_memory_bytes": prop.total_memory, "sm_count": prop.multi_processor_count,
+                  "driver_version": driver, "runtime_version": runtime, "cublas_version": base.version(),
+                  "suite": suite, "seed": seed, "repeats": repeats, "samples": samples, "timing": "cuda-graph-events",
+                  "cache_policy": "rotating-weight-copies-over-2x-L2",
+                  "transfer_timing": "h2d-input-kernel-d2h-output-events" if include_transfers else "omitted",
+                  "data": "captured-model-fixture" if captured is not None else "synthetic-fp16-model-shapes",
+                  "distribution": dist, "atol": ATOL, "rtol": RTOL,
+                  "hbm_peak_gbs": peaks["hbm_gbs"], "hbm_peak_source": peaks["source"], "cases": []}
+        for name, hidden, inter in cases:
+            w = Workload(torch, hidden, inter, seed, dist, device, fixture=captured)
+            for ffn in (False, True):
+                result["cases"].append(run_case(torch, L, base, w, name, ffn, ids, repeats, samples,
+                                                include_transfers, stream))
+            del w
+            torch.cuda.empty_cache()
+        base.close()
+        return result
+    finally:
+        torch.cuda.set_stream(prev)
 
 
 def main(argv=None):
