@@ -40,6 +40,9 @@ sys.path.insert(0, str(ROOT / "cuda-kernel_b200"))
 METRIC = "SwiGLU FFN µs/layer and % of HBM peak, batch 1 (4096→14336), 1/2/4/8 B200"
 UNIT = "us/layer"
 L2_BYTES = 126 * 1024 * 1024
+# NVLink 5 peer copy per direction per GPU measured on this pool's B200s (nominal 900 GB/s):
+# the denominator of the fused exchange's NVLink fraction.
+NVLINK_PEER_GBS = 770.0
 
 
 def parse():
@@ -109,7 +112,8 @@ def reference_arm(args) -> None:
         "config": {"workload": f"SwiGLU FFN {H}->{I} batch 1", "hidden": H, "intermediate": I, "batch": 1,
                    "parallelism": "host threads", "seed": 0},
         "cpu_baseline": {"value": us, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"{args.steps} full {H}->{I} layers (decode::matvec x3 + SiLU + residual), "
+                         "sample": f"{args.steps} full {H}->{I} layers (decode::matvec x3 + SiLU + residual; "
+                                   f"fp16->fp32 conversion of the weights included, block by block), "
                                    f"rows split over {threads} threads",
                          "median_step_us": statistics.median(samples) * 1e6},
         "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -159,17 +163,27 @@ def tune(torch, binding, launch_gate, launch_down, ids, stream, reps=8, down_ids
     return best
 
 
-def traffic_from_profile(kernel_tag: str, H: int, I: int):
-    """DRAM bytes per launch recorded by the committed ncu summary for this kernel/workload, if any
-    (the gate stage of a layer H -> I; a tensor-parallel shard's launch is that figure over N)."""
-    path = ROOT / "profiles" / f"{kernel_tag}_{H}x{I}.txt"
-    try:
-        for line in path.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(float(line.split(":", 1)[1].strip()))
-    except OSError:
-        pass
-    return None
+def traffic_from_profile(tag: str, cfg: int, H: int, I: int, shard: int, world: int):
+    """DRAM bytes (read + write) per launch of kernel `tag` at registry id `cfg`, from the committed
+    ncu summary of that kernel: profiles/<tag>_<H>x<rows>.txt holds one line
+    ``traffic_bytes_per_launch[<id>]: <bytes>`` per profiled geometry. A tensor-parallel shard
+    uses its own shape's summary when one exists, else the full layer's figure over N (weight
+    traffic scales with the shard). Returns (bytes or None, where it came from)."""
+    import re
+    cands = [(shard, 1)] if world > 1 else []
+    cands.append((I, world))
+    for rows, div in cands:
+        path = ROOT / "profiles" / f"{tag}_{H}x{rows}.txt"
+        try:
+            text = path.read_text()
+        except OSError:
+            continue
+        m = re.search(r"^traffic_bytes_per_launch\[%d\]:\s*([0-9.eE+]+)" % cfg, text, flags=re.M)
+        if m:
+            how = "ncu dram__bytes_read.sum + dram__bytes_write.sum"
+            return int(float(m.group(1)) // div), (f"{path.relative_to(ROOT)} ({how}, config {cfg}"
+                                                   + (f", full layer / {div}" if div > 1 else "") + ")")
+    return None, f"no committed ncu summary of {tag} config {cfg} at this shape"
 
 
 def cpu_baseline(sets, common, H, I, budget_s):
@@ -192,7 +206,8 @@ def cpu_baseline(sets, common, H, I, budget_s):
             break
     return {"value": el / n * 1e6, "unit": UNIT, "cores": 1, "kind": kind,
             "sample": f"{n} full {H}->{I} layers on 1 host thread (decode::matvec x3 + SiLU + residual, "
-                      f"as src/benchmark.cu:131-141), {el:.1f} s"}
+                      f"as src/benchmark.cu:131-141; fp16->fp32 conversion of the weights included, "
+                      f"block by block), {el:.1f} s"}
 
 
 def ours(args) -> None:
@@ -483,35 +498,56 @@ def ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         one_step_us = float(t.item())
 
-    # ---- dominant kernel: CUDA events around each launch, same rotating copies. With the
-    # fused layer kernel that is the one launch of the step; otherwise the gate kernel.
-    events = []
-    for i in range(args.steps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if lcfg:
-            a.record(stream)
-            step(i)
-            b.record(stream)
-        else:
-            a.record(stream)
-            launch_gate(gcfg, i)
-            b.record(stream)
-            launch_down(dcfg, i)
-        events.append((a, b))
-    torch.cuda.synchronize()
-    launch_us = statistics.mean(a.elapsed_time(b) * 1e3 for a, b in events)
+    # ---- each kernel alone: `kn` back-to-back launches over the rotating copies captured in
+    # one CUDA graph, in plain stream order (no programmatic overlap with a neighbour), timed
+    # with CUDA events on the launching stream around whole replays; per-launch time = replay
+    # time / kn (median of 3 replays, max over ranks). With the fused layer kernel the
+    # dominant kernel is that one launch per step; otherwise the gate kernel.
+    kn = copies * max(1, args.steps // copies)
+
+    def alone_us(launch):
+        for c in range(copies):
+            launch(c)
+        torch.cuda.synchronize()
+        g = capture(launch, 0, kn)
+        g.replay()
+        torch.cuda.synchronize()
+        t = statistics.median(time_kernel(torch, lambda i: g.replay(), 1, stream) for _ in range(3)) / kn
+        g.reset()
+        if world > 1:
+            tt = torch.tensor([t], dtype=torch.float64, device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
     peaks = intensity.measured_peaks(ROOT / "MEASURED_PEAKS.json")
-    kbytes, ktag = (rank_bytes, "layer") if lcfg else (gate_bytes, "gate")
-    achieved = kbytes / (launch_us * 1e-6) / 1e9
+    down_bytes = rank_bytes - gate_bytes
+
+    def kernel_record(tag, cfg, nbytes, us):
+        traffic, source = traffic_from_profile(tag, cfg, H, I, shard, world)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        return {"config": cfg, "launch_us": us, "bytes_per_launch": nbytes, "achieved": gbs,
+                "frac": gbs / peaks["hbm_gbs"], "traffic": traffic, "traffic_source": source,
+                "launches_timed": kn}
+
+    kernels = {}
+    if lcfg:
+        kernels["layer"] = kernel_record("layer", lcfg, rank_bytes,
+                                         alone_us(lambda i: layer_step(lcfg, gcfg, dcfg, i)))
+    kernels["gate"] = kernel_record("gate", gcfg, gate_bytes, alone_us(lambda i: launch_gate(gcfg, i)))
+    kernels["down"] = kernel_record("down", dcfg, down_bytes, alone_us(lambda i: launch_down(dcfg, i)))
+    dom = kernels["layer" if lcfg else "gate"]
     kname = (f"fused layer (config {lcfg})" + (" with the NVLink exchange" if world > 1 else "")) if lcfg \
         else f"gate (config {gcfg})"
-    roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                "peak_source": f"{peaks['source']} copy bandwidth",
-                "traffic": (lambda t: None if t is None else t // world)(traffic_from_profile(ktag, H, I)),
-                "traffic_source": "profiles/%s_%dx%d.txt (ncu, full layer; scaled by 1/N for a shard)" % (ktag, H, I),
-                "bytes_per_launch": kbytes,
-                "launch_us": launch_us}
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": dom["achieved"], "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": dom["frac"],
+                "peak_source": f"{peaks['source']} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+                               if peaks["source"] == "measured" else f"{peaks['source']} copy bandwidth",
+                "traffic": dom["traffic"], "traffic_source": dom["traffic_source"],
+                "bytes_per_launch": dom["bytes_per_launch"], "launch_us": dom["launch_us"],
+                "timing": f"{kn} back-to-back launches of the kernel alone in one CUDA graph, "
+                          "plain stream order, CUDA events around whole replays",
+                "kernels": kernels}
     layer_gbs = rank_bytes / (us_per_layer * 1e-6) / 1e9
     layer_roofline = {"achieved": layer_gbs, "frac": layer_gbs / peaks["hbm_gbs"], "unit": "GB/s",
                       "bytes_per_step_per_rank": rank_bytes}
@@ -552,10 +588,63 @@ def ours(args) -> None:
         del ag
         t = torch.tensor([ar], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl_ar = float(t.item())
+
+        # The exchange's own cost: the rank's step with the fused exchange against the same
+        # kernels with none (the partial y stays local), both as `kn` steps in one graph in
+        # plain stream order (no weight prefetch), max over ranks.
+        def step_local(i):
+            s = sets[i % copies]
+            if lcfg:
+                _lib.check(L.swb_ffn_fused(lcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                           x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
+                                           y.data_ptr(), H, shard, workspace.data_ptr(), sp))
+            else:
+                _lib.check(L.swb_ffn_tp(gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                        x.data_ptr(), bg.data_ptr(), bu.data_ptr(), h.data_ptr(), y.data_ptr(), H,
+                                        shard, sp))
+
+        def step_fused_plain(i):
+            s = sets[i % copies]
+            _lib.check(L.swb_ffn_tp_fused_ex(exchange.handle, lcfg or gcfg, 0 if lcfg else dcfg, s["wg"].data_ptr(),
+                                             s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(),
+                                             bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, shard,
+                                             0, sp))
+
+        def graph_step_us(fn):
+            for c in range(copies):
+                fn(c)
+            torch.cuda.synchronize()
+            g = capture(fn, 0, kn)
+            g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            v = statistics.median(time_kernel(torch, lambda i: g.replay(), 1, stream) for _ in range(3)) / kn
+            g.reset()
+            return v
+
+        local_us = graph_step_us(step_local)
+        fused_plain_us = graph_step_us(step_fused_plain)
+        t = torch.tensor([local_us, fused_plain_us], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        local_us, fused_plain_us = float(t[0]), float(t[1])
+        exchange_us = max(fused_plain_us - local_us, 1e-3)
+        # what must cross NVLink per rank and step: this rank's fp32 partial of every row to each
+        # peer (the payload), sent as 8-byte {value, epoch} words (the wire bytes)
+        payload = (world - 1) * H * 4
+        wire = (world - 1) * H * 8
+        nvlink = {"bytes_per_rank_step": payload, "wire_bytes_per_rank_step": wire, "exchange_us": exchange_us,
+                  "achieved": wire / (exchange_us * 1e-6) / 1e9, "peak": NVLINK_PEER_GBS, "unit": "GB/s",
+                  "frac": wire / (exchange_us * 1e-6) / 1e9 / NVLINK_PEER_GBS,
+                  "peak_source": "measured NVLink peer copy per direction on this pool's B200s",
+                  "how": "exchange_us = fused rank step - the same kernels without the exchange, each "
+                         f"{kn} steps in one CUDA graph without weight prefetch (max over ranks)",
+                  "local_step_us": local_us, "fused_step_no_prefetch_us": fused_plain_us,
+                  "latency_bound": True}
         tp = {"ranks": world, "shard_rows": shard, "exchange": "fused one-shot all-reduce over NVLink peer memory "
               "in the down kernel", "nccl_step_us": nccl_us, "fused_speedup_vs_nccl": nccl_us / us_per_layer,
               "nccl_one_step_graph_us": nccl_one,
-              "nccl_allreduce_us": float(t.item()), "allreduce_bytes": H * 4}
+              "nccl_allreduce_us": nccl_ar, "allreduce_bytes": H * 4, "nvlink_roofline": nvlink}
 
     # ---- end to end through the public C-ABI call with host buffers (N=1). As the
     # reference's transfer-inclusive timing (src/benchmark.cu:177-206): each step copies

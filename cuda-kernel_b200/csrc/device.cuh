@@ -205,7 +205,7 @@ __device__ __forceinline__ bool wait_slot(const unsigned long long* p, uint32_t 
 // ----------------------------------------------------------- activation
 
 // SiLU(v) = v / (1 + exp(-v)), written in two branches so exp never overflows
-// (the same stable form as include/kernels.cuh:39-42 of the reference).
+// (the same stable form as include/kernels.cuh:18-21 of the reference).
 __device__ __forceinline__ float silu(float v) {
     if (v >= 0.f) return v / (1.f + expf(-v));
     const float e = expf(v);

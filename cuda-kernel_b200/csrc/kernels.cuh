@@ -4,7 +4,7 @@
 // matrix with fp32 accumulation, optionally a second matrix U against the same
 // x (the gated SwiGLU stage), and writes one of three epilogues:
 //   MODE_GATE: h = fp16(SiLU(a + bg) * (b + bu)), optionally with the eager
-//              fp16 rounding points (kernels.cuh:123-127 of the reference);
+//              fp16 rounding points (kernels.cuh:102-106 of the reference);
 //   MODE_F32 : y = a (+ bias) (+ residual), fp32;
 //   MODE_F16 : the same rounded to fp16.
 // These replace decode::project (include/kernels.cuh:24-114 of shubhxho/cuda-kernel).
@@ -58,17 +58,21 @@ struct Params {
     uint32_t* epoch;
 };
 
-// In every kernel that can run as the gate of a tensor-parallel call, right after
-// its griddepcontrol.wait: one fire-and-forget add (no thread waits for it). The
-// previous call's down kernel, which read the epoch, has completed by then (even
-// when the gate was launched programmatically and started early); this call's
-// down kernel reads it only after its own griddepcontrol.wait, when this grid's
-// memory operations are complete. Epochs
-// start at 1 in a zeroed exchange, so a slot's epoch field is 0 only until its
-// first write; every call writes each slot a reader of its parity waits on, so
-// when the counter wraps back to 0 no such slot still holds that value.
-__device__ __forceinline__ void advance_call_epoch(const Params& p) {
-    if (p.epoch && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(p.epoch, 1u);
+// In every kernel that can run as the gate of a tensor-parallel call, after its
+// griddepcontrol.wait: one fire-and-forget add (no thread waits for it), made by
+// thread 0 of the one CTA that `owner` names -- the CTA that owns row 0 of the
+// output. For the families with a fixed row -> CTA map that is CTA 0; under work
+// stealing (sbulk_kernel) CTA 0 itself may be cancelled before it starts, so
+// there it is whichever CTA streams the stage holding row 0. The previous call's
+// down kernel, which read the epoch, has completed by then (even when the gate
+// was launched programmatically and started early); this call's down kernel
+// reads it only after its own griddepcontrol.wait, when this grid's memory
+// operations are complete. Epochs start at 1 in a zeroed exchange, so a slot's
+// epoch field is 0 only until its first write; every call writes each slot a
+// reader of its parity waits on, so when the counter wraps back to 0 no such
+// slot still holds that value.
+__device__ __forceinline__ void advance_call_epoch(const Params& p, bool owner) {
+    if (p.epoch && owner && threadIdx.x == 0) atomicAdd(p.epoch, 1u);
 }
 
 template <int MODE>
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(32 * WPR * ROWS) ldg_kernel(const Params p) {
     griddep_launch_dependents();
     // x may be the previous kernel's output (h of the gate stage).
     griddep_wait();
-    advance_call_epoch(p);
+    advance_call_epoch(p, blockIdx.x == 0);
     if (p.x_staged) {
         stage_x(p.x, xs, cols, threadIdx.x, blockDim.x);
         __syncthreads();
@@ -415,7 +419,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
-    advance_call_epoch(p);
+    advance_call_epoch(p, blockIdx.x == 0);
     stage_x(p.x, xs, cols, t, CT);
     named_barrier_sync(1, CT);
     float acc[NM][4];
@@ -649,7 +653,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
     if (epoch_out) {
         if (t == 0) *epoch_out = *reinterpret_cast<volatile const uint32_t*>(p.epoch);
     } else {
-        advance_call_epoch(p);
+        advance_call_epoch(p, blockIdx.x == 0);
     }
     float xr[MAXJ][8];
     const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
@@ -976,7 +980,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
-    advance_call_epoch(p);
     float xr[MAXJ][8];
     const bool x16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
 #pragma unroll
@@ -1010,6 +1013,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
         }
         const int2 m = meta[s];
         if (m.x < 0) break;
+        // row 0 is in exactly one stage of one CTA, whichever CTA took its block
+        advance_call_epoch(p, m.x == 0);
         const __half* sw = ring + size_t(s) * stage_halves;
         float* ps = part + size_t(s) * rs * CW * NM;
         for (int r = 0; r < m.y; ++r) {
@@ -1065,7 +1070,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
 
 // ============================================================== pointwise
 
-// kernels.cuh:155-162 of the reference: the cuBLAS path's gate epilogue.
+// kernels.cuh:134-141 of the reference: the cuBLAS path's gate epilogue.
 __global__ void gate_epilogue_kernel(const float* a, const float* b, const __half* bg, const __half* bu,
                                      __half* h, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1076,7 +1081,7 @@ __global__ void gate_epilogue_kernel(const float* a, const float* b, const __hal
     }
 }
 
-// kernels.cuh:163-166 of the reference: y += bias + x.
+// kernels.cuh:142-145 of the reference: y += bias + x.
 __global__ void residual_epilogue_kernel(float* y, const __half* bias, const __half* x, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] += __half2float(bias[i]) + __half2float(x[i]);

@@ -1,10 +1,10 @@
 // C ABI of the B200 SwiGLU decode layer (declarations: include/swiglu_b200.h).
 //
-// Argument guards mirror decode::launch (include/kernels.cuh:136-154) and the
+// Argument guards mirror decode::launch (include/kernels.cuh:115-133) and the
 // torch binding (src/torch_extension.cu:7-40) of shubhxho/cuda-kernel, in the
 // same order and with the same messages, and run before any CUDA call.
 // Dispatch is generated from the registry list (registry.h), as
-// include/kernels.cuh:145-153 generates it from DECODE_CONFIGS.
+// include/kernels.cuh:124-131 generates it from DECODE_CONFIGS.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -721,7 +721,9 @@ static __device__ __align__(256) __half g_noalloc_h[SWB_NOALLOC_MAX_INTER];
 
 std::atomic<void*> g_noalloc_ptr[64];
 
-// Device address of g_noalloc_h on the current device, looked up once per device.
+// Device address of g_noalloc_h on the current device, looked up once per device
+// and kept for the life of the process (a device reset, which may reload the module
+// elsewhere, needs a fresh process).
 int noalloc_workspace(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -834,6 +836,20 @@ int swb_tp_connect(swb_tp_t* tp, const void* handles) {
         tp->peer[q] = p;
     }
     tp->connected = true;
+    return SWB_OK;
+}
+
+int swb_tp_epoch(const swb_tp_t* tp, uint32_t* out) {
+    if (!tp || !out) return fail(SWB_E_INPUT, "null exchange or output");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != tp->device)
+        return fail(SWB_E_INPUT, "the current device is not the exchange's device");
+    uint32_t v = 0;
+    const void* ctr = static_cast<const char*>(tp->local) + tp->recv_bytes;
+    cudaError_t e = cudaDeviceSynchronize();  // calls on any stream have counted
+    if (e == cudaSuccess) e = cudaMemcpy(&v, ctr, sizeof v, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    *out = v;
     return SWB_OK;
 }
 

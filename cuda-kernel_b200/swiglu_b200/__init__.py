@@ -6,7 +6,7 @@ Host-side mirror of shubhxho/cuda-kernel's operator surface over the C ABI of
 * ``swiglu_out`` / ``swiglu`` / ``config_ids`` -- the torch binding
   (``src/torch_extension.cu``), same names, checks and errors;
 * ``gate`` / ``project`` / ``ffn`` -- the kernel launches of
-  ``decode::launch`` (``include/kernels.cuh:136-154``);
+  ``decode::launch`` (``include/kernels.cuh:115-133``);
 * ``CublasBaseline`` -- the cuBLAS GemmEx + pointwise comparison path.
 
 Importing this package does not need a GPU; calling a kernel does.

@@ -102,6 +102,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_tp_ipc_handle": ([_vp, _vp], _i),
         "swb_tp_connect": ([_vp, _vp], _i),
         "swb_tp_destroy": ([_vp], _i),
+        "swb_tp_epoch": ([_vp, ctypes.POINTER(ctypes.c_uint32)], _i),
         "swb_ffn_tp_fused": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, _vp], _i),
         "swb_ffn_tp_fused_ex": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, ctypes.c_uint, _vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),

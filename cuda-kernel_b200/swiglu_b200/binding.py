@@ -185,7 +185,7 @@ def ffn_tp(x: torch.Tensor, wg_shard: torch.Tensor, wu_shard: torch.Tensor, wd_s
 
 
 def residual_epilogue(y: torch.Tensor, bias: torch.Tensor, x: torch.Tensor, stream: int | None = None) -> None:
-    """y += bias + x (kernels.cuh:163-166); closes a tensor-parallel layer."""
+    """y += bias + x (kernels.cuh:142-145); closes a tensor-parallel layer."""
     s = _stream(y.device) if stream is None else stream
     with torch.cuda.device(y.device):
         _lib.check(_lib.lib().swb_residual_epilogue(y.data_ptr(), bias.data_ptr(), x.data_ptr(), y.numel(), s))

@@ -2,6 +2,8 @@
 
     python -m swiglu_b200.ncu_summary launches <launches.csv>     # per-kernel launches, time, share
     python -m swiglu_b200.ncu_summary report <file.ncu-rep>       # key counters of each captured launch
+    python -m swiglu_b200.ncu_summary traffic <metrics.csv> <reps> <id,id,...>
+        # DRAM bytes per launch of each geometry of a `profile` plan (launches in plan order)
 
 `launches` reads a `--metrics gpu__time_duration.sum --csv` log; `report` runs
 `ncu -i <rep> --page raw --csv` (no GPU needed) and prints the DRAM, L2, SM and
@@ -12,6 +14,7 @@ from __future__ import annotations
 import collections
 import csv
 import io
+import statistics
 import subprocess
 import sys
 
@@ -79,8 +82,51 @@ def report(path: str) -> str:
     return "\n".join(out)
 
 
+def _per_launch(path: str) -> list[dict]:
+    """Rows of a `--metrics ... --csv` log grouped by launch ID, in launch order."""
+    text = open(path, encoding="utf-8", errors="replace").read()
+    lines = text.splitlines()
+    start = next(i for i, l in enumerate(lines) if "Kernel Name" in l and "Metric Name" in l)
+    rows = list(csv.reader(io.StringIO("\n".join(lines[start:]))))
+    hdr = rows[0]
+    idc, k, m, v, u = (hdr.index(x) for x in ("ID", "Kernel Name", "Metric Name", "Metric Value", "Metric Unit"))
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
+    out = collections.OrderedDict()
+    for r in rows[1:]:
+        if len(r) <= v:
+            continue
+        d = out.setdefault(r[idc], {"kernel": r[k].split("(")[0]})
+        val = float(r[v].replace(",", ""))
+        if r[m] == "gpu__time_duration.sum":
+            d["us"] = val * _UNIT.get(r[u], 1.0)
+        else:
+            d[r[m]] = val * scale.get(r[u], 1.0)
+    return list(out.values())
+
+
+def traffic(path: str, reps: int, ids: list[int]) -> str:
+    """Per geometry of a profile plan (`reps` launches of each id, in order): mean DRAM read,
+    write and duration per launch, and the `traffic_bytes_per_launch[<id>]` line bench.py reads."""
+    launches_ = _per_launch(path)
+    if len(launches_) != reps * len(ids):
+        raise SystemExit(f"{len(launches_)} launches in the log, the plan has {reps} x {len(ids)}")
+    out = []
+    for n, cid in enumerate(ids):
+        block = launches_[n * reps:(n + 1) * reps]
+        rd = statistics.mean(b["dram__bytes_read.sum"] for b in block)
+        wr = statistics.mean(b["dram__bytes_write.sum"] for b in block)
+        us = statistics.mean(b["us"] for b in block) if all("us" in b for b in block) else float("nan")
+        out.append(f"config {cid}: {block[0]['kernel']}, {reps} launches: read {rd / 1e6:.3f} MB, "
+                   f"write {wr / 1e6:.3f} MB, {us:.2f} us (serialised)")
+        out.append(f"traffic_bytes_per_launch[{cid}]: {rd + wr:.0f}")
+    return "\n".join(out)
+
+
 def main(argv=None):
     argv = argv or sys.argv[1:]
+    if len(argv) == 4 and argv[0] == "traffic":
+        print(traffic(argv[1], int(argv[2]), [int(v) for v in argv[3].split(",") if v]))
+        return
     if len(argv) != 2 or argv[0] not in ("launches", "report"):
         raise SystemExit(__doc__)
     print(launches(argv[1]) if argv[0] == "launches" else report(argv[1]))

@@ -9,6 +9,12 @@ launches by index.
     python -m swiglu_b200.profile --gate-config 69 --down-config 67 --reps 20
     python -m swiglu_b200.profile --only gate --gate-config 69 --reps 6
     python -m swiglu_b200.profile --tp-ranks 8 --gate-config 69 --down-config 87 --reps 12
+    python -m swiglu_b200.profile --only gate --gate-config 68,69,79 --reps 4
+
+A comma-separated list of ids runs ``--reps`` launches of each geometry in turn
+(gate ids with ``--only gate``, down ids with ``--only down``); the plan is
+printed first, one line per geometry, so a launch list can be split by geometry
+in launch order (``ncu_summary traffic``).
 
 ``--tp-ranks n`` runs one tensor-parallel rank's layer (an intermediate shard
 of I/n rows) through swb_ffn_tp_fused on a one-rank exchange: the fused down +
@@ -25,8 +31,8 @@ def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--hidden", type=int, default=4096)
     p.add_argument("--intermediate", type=int, default=14336)
-    p.add_argument("--gate-config", type=int, default=69)
-    p.add_argument("--down-config", type=int, default=67)
+    p.add_argument("--gate-config", type=str, default="69", help="registry id, or ids (comma-separated)")
+    p.add_argument("--down-config", type=str, default="67", help="registry id, or ids (comma-separated)")
     p.add_argument("--reps", type=int, default=10)
     p.add_argument("--only", choices=("layer", "gate", "down"), default="layer")
     p.add_argument("--tp-ranks", type=int, default=0, help="profile one rank's fused layer at I / n rows")
@@ -37,6 +43,16 @@ def main():
     from swiglu_b200 import _lib
 
     H, I = a.hidden, a.intermediate
+    gate_ids = [int(v) for v in a.gate_config.split(",") if v]
+    down_ids = [int(v) for v in a.down_config.split(",") if v]
+    if a.only == "gate":
+        plan = [(g, down_ids[0]) for g in gate_ids]
+    elif a.only == "down":
+        plan = [(gate_ids[0], d) for d in down_ids]
+    else:
+        if len(gate_ids) != len(down_ids):
+            raise SystemExit("a layer plan needs as many gate ids as down ids")
+        plan = list(zip(gate_ids, down_ids))
     if a.tp_ranks:
         if I % a.tp_ranks:
             raise SystemExit("intermediate size must divide by --tp-ranks")
@@ -71,29 +87,31 @@ def main():
     if a.tp_ranks:
         from swiglu_b200.tp import Exchange
         ex = Exchange(0, 1, H, dev)
+    for k, (gc, dc) in enumerate(plan):
+        print(f"plan {k}: {a.reps} x {a.only} gate {gc} down {dc}", flush=True)
     with torch.cuda.stream(stream):
-        for i in range(a.reps):
-            s = sets[i % copies]
-            if ex is not None:
-                rc = L.swb_ffn_tp_fused(ex.handle, a.gate_config, a.down_config, s["wg"].data_ptr(), s["wu"].data_ptr(),
-                                        s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(),
-                                        h.data_ptr(), y.data_ptr(), H, I, sp)
-            elif a.only == "layer":
-                rc = L.swb_ffn(a.gate_config, a.down_config, s["wg"].data_ptr(), s["wu"].data_ptr(),
-                               s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(),
-                               h.data_ptr(), y.data_ptr(), H, I, sp)
-            elif a.only == "gate":
-                rc = L.swb_gate(a.gate_config, s["wg"].data_ptr(), s["wu"].data_ptr(), x.data_ptr(), bg.data_ptr(),
-                                bu.data_ptr(), h.data_ptr(), I, H, 0, sp)
-            else:
-                rc = L.swb_project(a.down_config, s["wd"].data_ptr(), h.data_ptr(), bd.data_ptr(), x.data_ptr(),
-                                   y.data_ptr(), H, I, _lib.SWB_RESIDUAL, sp)
-            _lib.check(rc)
+        for gc, dc in plan:
+            for i in range(a.reps):
+                s = sets[i % copies]
+                if ex is not None:
+                    rc = L.swb_ffn_tp_fused(ex.handle, gc, dc, s["wg"].data_ptr(), s["wu"].data_ptr(),
+                                            s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(), bu.data_ptr(),
+                                            bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, I, sp)
+                elif a.only == "layer":
+                    rc = L.swb_ffn(gc, dc, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(),
+                                   bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, I, sp)
+                elif a.only == "gate":
+                    rc = L.swb_gate(gc, s["wg"].data_ptr(), s["wu"].data_ptr(), x.data_ptr(), bg.data_ptr(),
+                                    bu.data_ptr(), h.data_ptr(), I, H, 0, sp)
+                else:
+                    rc = L.swb_project(dc, s["wd"].data_ptr(), h.data_ptr(), bd.data_ptr(), x.data_ptr(),
+                                       y.data_ptr(), H, I, _lib.SWB_RESIDUAL, sp)
+                _lib.check(rc)
     torch.cuda.synchronize()
     if ex is not None:
         ex.close()
-    print(f"ran {a.reps} x {a.only} {H}->{I} (configs {a.gate_config}/{a.down_config}"
-          f"{', fused tensor-parallel rank' if ex is not None else ''}), {copies} copies")
+    print(f"ran {a.reps} x {a.only} {H}->{I} for each of {len(plan)} geometries"
+          f"{' (fused tensor-parallel rank)' if ex is not None else ''}, {copies} copies")
 
 
 if __name__ == "__main__":

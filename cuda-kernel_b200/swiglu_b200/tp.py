@@ -72,6 +72,13 @@ class Exchange:
     def handle(self):
         return self._ptr
 
+    def epoch(self) -> int:
+        """Calls this rank's exchange has counted (synchronises the device)."""
+        out = ctypes.c_uint32()
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().swb_tp_epoch(self._ptr, ctypes.byref(out)))
+        return out.value
+
     def close(self) -> None:
         if self._ptr is not None and self._ptr.value:
             with torch.cuda.device(self.device):

@@ -322,10 +322,12 @@ def run(suite="decode", repeats=100, samples=9, seed=17, dist="normal", include_
     elif hidden or intermediate:
         raise ValueError("custom dimensions require --fixture")
     device = torch.device("cuda", device_index)
+    prev_device = torch.cuda.current_device()
     torch.cuda.set_device(device)
     stream = torch.cuda.Stream(device)
     prev = torch.cuda.current_stream(device)
-    torch.cuda.set_stream(stream)  # the caller's stream comes back on the way out
+    torch.cuda.set_stream(stream)  # the caller's stream and device come back on the way out
+    base = None
     try:
         L = _lib.lib()
         base = CublasBaseline(device)
@@ -350,10 +352,12 @@ def run(suite="decode", repeats=100, samples=9, seed=17, dist="normal", include_
                                                 include_transfers, stream))
             del w
             torch.cuda.empty_cache()
-        base.close()
         return result
     finally:
+        if base is not None:
+            base.close()
         torch.cuda.set_stream(prev)
+        torch.cuda.set_device(prev_device)
 
 
 def main(argv=None):

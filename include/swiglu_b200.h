@@ -30,12 +30,12 @@ extern "C" {
 
 /* ---- status codes; swb_status_string() gives the reference's message ---- */
 #define SWB_OK 0
-#define SWB_E_INPUT 1          /* "invalid projection input"      include/kernels.cuh:140 */
-#define SWB_E_GATE_BUFFERS 2   /* "invalid gate buffers"          include/kernels.cuh:141 */
-#define SWB_E_HALF_OUTPUT 3    /* "missing half output"           include/kernels.cuh:142 */
-#define SWB_E_FLOAT_OUTPUT 4   /* "missing float output"          include/kernels.cuh:143 */
-#define SWB_E_RESIDUAL 5       /* "missing residual"              include/kernels.cuh:144 */
-#define SWB_E_CONFIG 6         /* "unknown kernel configuration"  include/kernels.cuh:151, config.hpp:19 */
+#define SWB_E_INPUT 1          /* "invalid projection input"      include/kernels.cuh:119 */
+#define SWB_E_GATE_BUFFERS 2   /* "invalid gate buffers"          include/kernels.cuh:120 */
+#define SWB_E_HALF_OUTPUT 3    /* "missing half output"           include/kernels.cuh:121 */
+#define SWB_E_FLOAT_OUTPUT 4   /* "missing float output"          include/kernels.cuh:122 */
+#define SWB_E_RESIDUAL 5       /* "missing residual"              include/kernels.cuh:123 */
+#define SWB_E_CONFIG 6         /* "unknown kernel configuration"  include/kernels.cuh:130, config.hpp:19 */
 #define SWB_E_SHAPE 7          /* "invalid shape"                 src/torch_extension.cu:17 */
 #define SWB_E_CONFIG_RANGE 8   /* "configuration out of range"    src/torch_extension.cu:21 */
 #define SWB_E_CONFIG_INVALID 9 /* "invalid configuration"         src/torch_extension.cu:22 */
@@ -47,7 +47,7 @@ extern "C" {
 #define SWB_E_WORKSPACE 15     /* size beyond the built-in workspace of swb_ffn_noalloc; a missing
                                   or misaligned swb_ffn_fused workspace */
 
-/* project() flags (template flags of decode::launch, include/kernels.cuh:136) */
+/* project() flags (template flags of decode::launch, include/kernels.cuh:115) */
 #define SWB_RESIDUAL 1u /* add residual[row] after bias (RESIDUAL) */
 #define SWB_HALF_OUT 2u /* write fp16 into out instead of fp32 (HALF_OUT) */
 
@@ -86,12 +86,12 @@ SWB_API int swb_valid_config(int64_t id);
 /* config.hpp:17-20 config(id); SWB_E_CONFIG for unknown ids. */
 SWB_API int swb_config_info(int64_t id, swb_config_t* out);
 
-/* ---- kernels: replace decode::launch<GATED,RESIDUAL,HALF_OUT,MODEL_ROUND>, kernels.cuh:136-154 ---- */
+/* ---- kernels: replace decode::launch<GATED,RESIDUAL,HALF_OUT,MODEL_ROUND>, kernels.cuh:115-133 ---- */
 
 /* launch<true,false,false,MODEL_ROUND>: h[i] = fp16(SiLU(Wg[i].x + bg[i]) * (Wu[i].x + bu[i])).
  * Wg, Wu: [rows, cols] row-major fp16; x: [cols]; bg, bu: [rows] or NULL; h: [rows] fp16.
  * model_round != 0 rounds to fp16 after each dot, after SiLU and after the product
- * (kernels.cuh:123-127), matching eager fp16 Linear -> SiLU -> multiply. */
+ * (kernels.cuh:102-106), matching eager fp16 Linear -> SiLU -> multiply. */
 SWB_API int swb_gate(int config, const void* wg, const void* wu, const void* x, const void* bg, const void* bu,
              void* h, int rows, int cols, int model_round, void* stream);
 
@@ -118,7 +118,9 @@ SWB_API int swb_ffn(int gate_config, int down_config, const void* wg, const void
  * and y. Nothing is allocated: no cudaMalloc/cudaFree and no library routine
  * that allocates. inter > SWB_NOALLOC_MAX_INTER returns SWB_E_WORKSPACE.
  * The first call on a device looks up that device's copy of the array
- * (cudaGetSymbolAddress) -- make it before any stream capture on that device.
+ * (cudaGetSymbolAddress) and keeps its address for the life of the process --
+ * make that first call before any stream capture on that device. A reset of the
+ * device (cudaDeviceReset) may move the array: use a fresh process after one.
  * Every call shares the one array: h is fully rewritten by each call, so nothing
  * needs clearing, but calls that may overlap on the GPU (other streams, other
  * threads) race on it and must be serialised by the caller. */
@@ -176,6 +178,11 @@ SWB_API int swb_tp_create(int rank, int world, int rows, swb_tp_t** out);
 SWB_API int swb_tp_ipc_handle(const swb_tp_t* tp, void* out);
 SWB_API int swb_tp_connect(swb_tp_t* tp, const void* handles);
 SWB_API int swb_tp_destroy(swb_tp_t* tp);
+/* Calls this rank's exchange has counted so far (the call epoch; every call,
+ * fused layer or two-kernel, advances it exactly once). Synchronises the
+ * device. After a device error, ranks whose counts differ show which rank
+ * fell behind. */
+SWB_API int swb_tp_epoch(const swb_tp_t* tp, uint32_t* out);
 /* One rank's whole layer: gate on its shard, then the fused down + all-reduce;
  * y: [hidden] fp32, identical on every rank. down_config must be an RBULK id;
  * when its rows cannot hold the shard's columns, RBULK 87, 85 or 82 runs instead.
@@ -212,7 +219,7 @@ SWB_API int swb_swiglu_out(const void* x, const void* gate, const void* up, cons
                    int64_t hidden, int64_t intermediate, int64_t gate_config, int64_t down_config,
                    void* stream);
 
-/* ---- pointwise kernels of the cuBLAS path: kernels.cuh:155-166 ---- */
+/* ---- pointwise kernels of the cuBLAS path: kernels.cuh:134-145 ---- */
 /* gate_epilogue: h[i] = fp16(SiLU(a[i] + bg[i]) * (b[i] + bu[i])) */
 SWB_API int swb_gate_epilogue(const float* a, const float* b, const void* bg, const void* bu, void* h, int n,
                       void* stream);

@@ -5,7 +5,7 @@
  * Replaces Workload::gemv / Workload::baseline of shubhxho/cuda-kernel
  * (src/benchmark.cu:143-160): three cublasGemmEx calls (fp16 in, fp32 out,
  * CUBLAS_COMPUTE_32F, algorithm DEFAULT or DEFAULT_TENSOR_OP) and the two
- * pointwise epilogues (include/kernels.cuh:155-166).
+ * pointwise epilogues (include/kernels.cuh:134-145).
  * Library: cuda-kernel_b200/lib/libswiglu_b200_cublas.so. Status codes are the
  * SWB_* codes of swiglu_b200.h; SWBL_E_CUBLAS carries a cuBLAS failure.
  */

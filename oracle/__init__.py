@@ -28,7 +28,9 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "lib" / "libswiglu_oracle.so"
 REF_PATH = HERE / "_ref" / "libswiglu_ref.so"
-REFERENCE_TREE = Path(os.environ.get("SWIGLU_REFERENCE_TREE", "/root/reference"))
+# The reference checkout: $SWIGLU_REFERENCE_TREE, else a `reference/` directory beside
+# this repository's own directory (absent on machines that only run the prebuilt files).
+REFERENCE_TREE = Path(os.environ.get("SWIGLU_REFERENCE_TREE") or (HERE.parents[1] / "reference"))
 
 _u16p = ctypes.POINTER(ctypes.c_uint16)
 _f32p = ctypes.POINTER(ctypes.c_float)

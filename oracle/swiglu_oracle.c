@@ -225,7 +225,7 @@ done:
 
 static inline float round16(float v) { return g_f16_table[orc_f32_to_f16(v)]; }
 
-/* kernels.cuh:119-128 gate epilogue. Without model rounding it uses the FFN
+/* kernels.cuh:98-107 gate epilogue. Without model rounding it uses the FFN
  * reference's double-precision activation (benchmark.cu:136-138). */
 int orc_gate(const uint16_t* wg, const uint16_t* wu, const uint16_t* x, const uint16_t* bg,
              const uint16_t* bu, int rows, int cols, int model_round, uint16_t* h) {
@@ -261,7 +261,7 @@ done:
     return rc;
 }
 
-/* kernels.cuh:119-132 plain epilogue: a += bias; a += residual; fp32 or fp16 out. */
+/* kernels.cuh:98-99,108-111 plain epilogue: a += bias; a += residual; fp32 or fp16 out. */
 int orc_project(const uint16_t* w, const uint16_t* x, const uint16_t* bias, const uint16_t* residual,
                 int rows, int cols, float* y, uint16_t* yh) {
     if (rows <= 0 || cols <= 0 || !w || !x || (!y && !yh)) return ORC_EINVAL;

@@ -14,7 +14,7 @@
  *   src/benchmark.cu:89-94       random_half (std::mt19937 + uniform_real_distribution<float>)
  *   src/benchmark.cu:116-121     workload generation order and scales
  *   src/benchmark.cu:131-141     FFN reference (projection, fp16 activation, residual output)
- *   include/kernels.cuh:123-131  model-rounding gate and half-output down (torch binding path)
+ *   include/kernels.cuh:102-106,110  model-rounding gate and half-output down (torch binding path)
  * Half-precision values travel as raw IEEE binary16 bit patterns (uint16_t).
  */
 #ifndef SWIGLU_ORACLE_H
@@ -65,7 +65,7 @@ int orc_ffn(const uint16_t* wg, const uint16_t* wu, const uint16_t* wd, const ui
             float* proj, uint16_t* act, float* y);
 
 /*
- * Model-rounding path of the torch binding (kernels.cuh:123-131 via torch_extension.cu:34-38):
+ * Model-rounding path of the torch binding (kernels.cuh:102-106,110 via torch_extension.cu:34-38):
  *   a = fp16(dot(Wg,x)), b = fp16(dot(Wu,x)), s = fp16(silu(a)), h = fp16(s*b), y = fp16(dot(Wd,h)).
  * Dots are double-accumulated and rounded to float first; silu and the product in float.
  */

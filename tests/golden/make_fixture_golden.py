@@ -40,7 +40,7 @@ def write_sources():
 
 def main():
     p = argparse.ArgumentParser(description=__doc__)
-    p.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    p.add_argument("--reference", type=Path, required=True, help="the reference checkout (read only)")
     a = p.parse_args()
     write_sources()
     exporter = a.reference / "tools" / "export_ffn.py"

@@ -208,6 +208,32 @@ def test_fused_tp_prefetch_chain_matches_plain(gcfg):
     ex.close()
 
 
+@pytest.mark.gpu
+def test_every_call_advances_the_exchange_epoch_once():
+    """Each fused tensor-parallel call advances the exchange's call epoch exactly once,
+    whichever gate family runs it. Under work stealing (SBULK ids) the CTA that owns row 0
+    does it, not CTA 0 (which the hardware may cancel before it starts): 200 back-to-back
+    calls per gate, no host synchronisation between them, must count 200."""
+    from swiglu_b200 import binding
+    from swiglu_b200 import tp as T
+    H, I, n = 4096, 14336, 8
+    dev = torch.device("cuda", 0)
+    w = O.normal_workload(0, H, I)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    s = T.shard(t(w["wg"]), t(w["wu"]), t(w["wd"]), t(w["bg"]), t(w["bu"]), 2, n)
+    x, bd = t(w["x"]), t(w["bd"])
+    h = torch.empty(I // n, dtype=torch.float16, device=dev)
+    y = torch.empty(H, dtype=torch.float32, device=dev)
+    ex = T.Exchange(0, 1, H, dev)
+    for gate in (96, 92, 99, 69, 33, 87, 200):
+        before = ex.epoch()
+        for _ in range(200):
+            T.ffn_tp_fused(ex, x, s, bd, h, y, gate, 87)
+        assert ex.epoch() - before == 200, gate
+    assert binding.device_error() == 0
+    ex.close()
+
+
 def _handles_worker(rank, world, port, mode, q):
     import datetime
     import time

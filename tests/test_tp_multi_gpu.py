@@ -4,9 +4,10 @@ Each rank runs swb_ffn_tp on its shard (rows of Wg/Wu, columns of Wd), the fp32
 partial y is summed with an NCCL all-reduce, and bias + residual are applied once
 (swb_residual_epilogue); then the fused paths (swb_ffn_tp_fused: the down kernel
 or the whole-layer kernel sums the partials over NVLink peer memory), including
-calls of different geometries issued back to back. Every rank's y is compared
-with the unsharded CPU oracle at the parity tests' tolerance, and the ranks' y
-must be bit-identical. Needs at least 2 GPUs; skipped otherwise.
+calls of different geometries issued back to back and the exchange's call count
+after them. Every rank's y is compared with the unsharded CPU oracle at the
+parity tests' tolerance, and the ranks' y must be bit-identical. Runs at 2, 4 and
+8 ranks, each skipped when the process sees fewer GPUs.
 """
 import os
 import socket
@@ -99,13 +100,21 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
         g.reset()
     torch.cuda.synchronize()
     assert all(torch.equal(yk, plain) for yk in chain_ys)
+    # every call advanced the exchange's epoch once on every rank, whichever gate ran it
+    # (SBULK work stealing included): 100 back-to-back calls, no host synchronisation
+    before = ex.epoch()
+    for k in range(100):
+        T.ffn_tp_fused(ex, x, s, bd, h, y, (96, 69, 92, 200)[k % 4], 87)
+    assert ex.epoch() - before == 100
+    torch.cuda.synchronize()
+    out.append(y.cpu().numpy().copy())
     dist.barrier()
     assert binding.device_error() == 0
     ex.close()
     q.put((rank, out))
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_nccl_matches_oracle(world):
     import torch
     if torch.cuda.device_count() < world:
@@ -134,5 +143,6 @@ def test_tp_nccl_matches_oracle(world):
         for y in results[rank]:
             assert np.max(np.abs(y - y_ref) / (np.abs(y_ref) + atol)) <= 2e-3
             assert O.compare(y, y_ref)[0]
-    for y0, y1 in zip(results[0], results[1]):
-        assert np.array_equal(y0, y1)  # every rank holds the same reduced y
+    for rank in range(1, world):
+        for y0, yr in zip(results[0], results[rank]):
+            assert np.array_equal(y0, yr)  # every rank holds the same reduced y

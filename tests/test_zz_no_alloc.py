@@ -6,10 +6,14 @@ a fixed array inside the library instead of a workspace argument. This file is
 named to be collected last; it must pass alone in a fresh process and after the
 other tests.
 
-Checked through the C ABI: two calls in a row, each against swb_ffn (the entry
-point that takes a caller workspace) with the y tolerance the parity tests use
-(relative error |a - e| / (|e| + atol_j) <= 2e-3, atol_j = 2^-11 sum_i |Wd[j,i] h[i]|);
-sizes beyond the array are rejected with a clear error before anything runs.
+Checked through the C ABI on two calls in a row with different inputs:
+* against swb_ffn (the entry point that takes a caller workspace): bit-identical,
+  the same kernels in the same order;
+* against the CPU oracle: y within the parity tests' tolerance of the oracle's
+  down projection of the kernels' h (relative error |a - e| / (|e| + atol_j) <= 2e-3,
+  atol_j = 2^-11 sum_i |Wd[j,i] h[i]|), and within the reference's own gate
+  (atol .003, rtol .01) of the oracle's whole layer.
+Sizes beyond the array are rejected with a clear error before anything runs.
 """
 import numpy as np
 import pytest
@@ -54,18 +58,30 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
         w = O.normal_workload(seed, hidden, inter)
         d = {k: _dev(v) for k, v in w.items()}
         h = torch.empty(inter, dtype=torch.float16, device="cuda")
-        _, act, _ = O.ffn(w)
+        _, _, y_ref = O.ffn(w)
         for cfg in cfgs:
             y_ws = _run("swb_ffn", cfg, d, hidden, inter, h)
+            h_k = h.cpu().numpy()  # the kernels' h (the no-alloc call writes the same into its array)
             y_na = _run("swb_ffn_noalloc", cfg, d, hidden, inter)
-            assert _y_tol_ok(y_na, y_ws, w["wd"], act), (shape, seed, cfg)
-            assert np.array_equal(y_na.view(np.uint32), y_ws.view(np.uint32))  # same kernels, same order
+            assert np.array_equal(y_na.view(np.uint32), y_ws.view(np.uint32)), (shape, seed, cfg)
+            y_own = O.project(w["wd"], h_k, w["bd"], w["x"])
+            assert _y_tol_ok(y_na, y_own, w["wd"], h_k), (shape, seed, cfg)
+            assert O.compare(y_na, y_ref)[0], (shape, seed, cfg)
 
 
 def test_noalloc_rejects_sizes_beyond_its_array():
+    """inter one past the array: rejected before any launch. Real buffers of that size are
+    passed, so a regression in the guard fails the assertion instead of reading bad memory."""
     L = _lib.lib()
-    fake = 0x7F0000000000
-    rc = L.swb_ffn_noalloc(33, 33, fake, fake, fake, fake, None, None, None, fake, 64,
-                           _lib.SWB_NOALLOC_MAX_INTER + 1, None)
+    hidden, inter = 64, _lib.SWB_NOALLOC_MAX_INTER + 1
+    wg = torch.zeros(inter, hidden, dtype=torch.float16, device="cuda")
+    wu = torch.zeros_like(wg)
+    wd = torch.zeros(hidden, inter, dtype=torch.float16, device="cuda")
+    x = torch.zeros(hidden, dtype=torch.float16, device="cuda")
+    y = torch.full((hidden,), 3.0, dtype=torch.float32, device="cuda")
+    rc = L.swb_ffn_noalloc(33, 33, wg.data_ptr(), wu.data_ptr(), wd.data_ptr(), x.data_ptr(), None, None, None,
+                           y.data_ptr(), hidden, inter, None)
     assert rc == _lib.SWB_E_WORKSPACE
     assert "65536" in _lib.last_error()
+    torch.cuda.synchronize()
+    assert bool(torch.all(y == 3.0))  # nothing ran
