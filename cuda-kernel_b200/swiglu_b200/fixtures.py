@@ -113,9 +113,11 @@ def as_layer(arrays: dict) -> dict:
 
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description="Export one captured SwiGLU layer, without executing pickle.")
-    p.add_argument("--weights", type=Path, required=True, help="local safetensors shard containing this layer")
-    p.add_argument("--prefix", required=True, help="e.g. model.layers.0.mlp")
-    p.add_argument("--input", type=Path, required=True, help="captured post-norm FFN input, one token .npy")
+    p.add_argument("--weights", type=Path, required=True,
+                   help="a safetensors file on disk that holds the layer's gate, up and down weights")
+    p.add_argument("--prefix", required=True, help="tensor-name prefix of the layer, such as model.layers.0.mlp")
+    p.add_argument("--input", type=Path, required=True,
+                   help=".npy of one token's input to the MLP, taken after the layer norm")
     p.add_argument("--output", type=Path, required=True)
     a = p.parse_args(argv)
     m = export(a.weights, a.prefix, a.input, a.output)

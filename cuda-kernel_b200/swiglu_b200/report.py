@@ -1,13 +1,24 @@
-"""Validate kernel-benchmark evidence (schema v1) and render a conservative comparison.
+"""Kernel evidence (schema v1): check every claim against its raw samples, then render it.
 
-Same contract as tools/report.py of shubhxho/cuda-kernel (:9-111): a report is
-rejected for an unknown schema or timing protocol, unknown data provenance,
-missing GPU identity or versions, fewer than 3 holdout samples, duplicate or
-unknown cases, non-positive timings, non-finite or failing correctness evidence,
-medians that do not match their raw samples, or a speedup that does not match
-the medians. A "separated win" needs a median speedup >= 1.05 and every custom
-sample below every baseline sample (:82-84). Rendering adds the B200 roofline:
-algorithmic bytes per case and the achieved fraction of the HBM peak.
+A tuner result (``swiglu_b200.tuner``) is accepted only when all of this holds,
+and every violation found is listed in one error:
+
+* header -- schema 1 with CUDA-graph event timing, a known data provenance, a
+  GPU name, positive integer driver / runtime / cuBLAS versions and repeat and
+  sample counts, at least three holdout samples per candidate;
+* cases -- each (shape, operation) once, a known operation, positive integer
+  dimensions;
+* each side (custom and cuBLAS) -- marked correct, finite non-negative error
+  figures with the scaled error within tolerance (<= 1), exactly ``samples``
+  positive finite timings whose median is the recorded median;
+* the recorded speedup equals baseline median / custom median, and any
+  transfer-inclusive timings obey the same sample rules.
+
+The verdict of a case is a "separated win" only when the median speedup is at
+least 1.05 and the custom kernel's slowest sample beats the baseline's fastest
+(the rule the reference's report states); "slower" below parity, otherwise
+"inconclusive". Rendering adds the B200 roofline of each case: algorithmic
+bytes, achieved GB/s and the fraction of the HBM copy peak.
 """
 from __future__ import annotations
 
@@ -21,136 +32,193 @@ from . import intensity
 
 DATA = ("synthetic-fp16-model-shapes", "captured-model-fixture")
 OPERATIONS = ("projection", "swiglu-ffn")
+SIDES = ("custom", "baseline")
+WIN_RATIO = 1.05
+
+
+class EvidenceError(ValueError):
+    """Raised with every problem found in a report."""
 
 
 def positive(v) -> bool:
-    return isinstance(v, (float, int)) and not isinstance(v, bool) and math.isfinite(v) and v > 0
+    return isinstance(v, (int, float)) and not isinstance(v, bool) and math.isfinite(v) and v > 0
+
+
+def _count(v) -> bool:
+    return positive(v) and isinstance(v, int)
+
+
+def _same(a, b) -> bool:
+    return positive(a) and positive(b) and math.isclose(a, b, rel_tol=1e-7)
+
+
+def _timings(where: str, block, n: int) -> list[str]:
+    """Rules for one list of samples and its median."""
+    if not isinstance(block, dict):
+        return [f"{where}: no timing block"]
+    xs = block.get("samples_us")
+    if not isinstance(xs, list) or len(xs) != n:
+        return [f"{where}: expected {n} samples"]
+    if not all(positive(x) for x in xs):
+        return [f"{where}: a sample is not a positive finite time"]
+    if not _same(block.get("median_us"), statistics.median(xs)):
+        return [f"{where}: recorded median is not the median of its samples"]
+    return []
+
+
+def _side(where: str, c, n: int) -> list[str]:
+    if not isinstance(c, dict):
+        return [f"{where}: missing"]
+    out = [] if c.get("correct") is True else [f"{where}: not marked correct"]
+    for key in ("max_abs_error", "max_scaled_error"):
+        v = c.get(key)
+        if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v) or v < 0:
+            out.append(f"{where}: {key} is not a finite non-negative number")
+        elif key == "max_scaled_error" and v > 1:
+            out.append(f"{where}: outside the numeric tolerance (scaled error {v:g})")
+    return out + _timings(where, c, n)
+
+
+def problems(report: dict) -> list[str]:
+    """Every rule the report breaks (empty when it is valid evidence)."""
+    if not isinstance(report, dict):
+        return ["not a JSON object"]
+    out = []
+    if report.get("schema_version") != 1:
+        out.append("schema_version is not 1")
+    if report.get("timing") != "cuda-graph-events":
+        out.append("timing protocol is not cuda-graph-events")
+    if report.get("data") not in DATA:
+        out.append(f"data provenance {report.get('data')!r} is not one of {DATA}")
+    if not report.get("gpu"):
+        out.append("no GPU identity")
+    for key in ("driver_version", "runtime_version", "cublas_version", "repeats", "samples"):
+        if not _count(report.get(key)):
+            out.append(f"{key} is not a positive integer")
+    n = report.get("samples")
+    if _count(n) and n < 3:
+        out.append("fewer than 3 holdout samples")
+    cases = report.get("cases")
+    if not isinstance(cases, list) or not cases:
+        return out + ["no cases"]
+    idents = [(c.get("shape"), c.get("operation")) for c in cases if isinstance(c, dict)]
+    if len(idents) != len(cases):
+        out.append("a case is not an object")
+    if len(set(idents)) != len(idents):
+        out.append("the same (shape, operation) appears twice")
+    for c in (c for c in cases if isinstance(c, dict)):
+        tag = f"{c.get('shape')}/{c.get('operation')}"
+        if c.get("operation") not in OPERATIONS:
+            out.append(f"{tag}: unknown operation")
+        if not (_count(c.get("hidden")) and _count(c.get("intermediate"))):
+            out.append(f"{tag}: dimensions are not positive integers")
+        for side in SIDES:
+            out += _side(f"{tag} {side}", c.get(side), n)
+        try:
+            ratio = c["baseline"]["median_us"] / c["custom"]["median_us"]
+            if not _same(ratio, c.get("speedup")):
+                out.append(f"{tag}: speedup is not baseline median / custom median")
+        except (KeyError, TypeError, ZeroDivisionError):
+            out.append(f"{tag}: speedup cannot be recomputed")
+        tr = c.get("transfer_inclusive")
+        if tr is not None:
+            for side in SIDES:
+                out += _timings(f"{tag} transfer-inclusive {side}", tr.get(side) if isinstance(tr, dict) else None, n)
+    return out
 
 
 def validate(report: dict) -> dict:
-    if report.get("schema_version") != 1 or report.get("timing") != "cuda-graph-events":
-        raise ValueError("unsupported benchmark schema or timing protocol")
-    if report.get("data") not in DATA:
-        raise ValueError("unknown data provenance")
-    if not report.get("gpu") or not report.get("cases"):
-        raise ValueError("missing GPU identity or workload cases")
-    for key in ("driver_version", "runtime_version", "cublas_version", "repeats", "samples"):
-        if not positive(report.get(key)) or not isinstance(report[key], int):
-            raise ValueError(f"missing or invalid {key}")
-    if report["samples"] < 3:
-        raise ValueError("insufficient holdout samples")
-    seen = set()
-    for case in report["cases"]:
-        ident = (case.get("shape"), case.get("operation"))
-        if ident in seen:
-            raise ValueError("duplicate benchmark case")
-        seen.add(ident)
-        if case.get("operation") not in OPERATIONS:
-            raise ValueError("unknown benchmark operation")
-        for key in ("hidden", "intermediate"):
-            if not positive(case.get(key)) or not isinstance(case[key], int):
-                raise ValueError("invalid workload dimensions")
-        for side in ("custom", "baseline"):
-            c = case[side]
-            values = c["samples_us"]
-            if c.get("correct") is not True or len(values) != report["samples"]:
-                raise ValueError("incorrect or incomplete candidate")
-            if not all(positive(v) for v in values):
-                raise ValueError("invalid GPU event timings")
-            for key in ("max_abs_error", "max_scaled_error"):
-                v = c.get(key)
-                if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v) or v < 0:
-                    raise ValueError("invalid correctness evidence")
-            if c["max_scaled_error"] > 1:
-                raise ValueError("numeric tolerance failed")
-            if not math.isclose(c["median_us"], statistics.median(values), rel_tol=1e-7):
-                raise ValueError("median does not match raw samples")
-        ratio = case["baseline"]["median_us"] / case["custom"]["median_us"]
-        if not math.isclose(ratio, case["speedup"], rel_tol=1e-7):
-            raise ValueError("speedup does not match timings")
-        transfer = case.get("transfer_inclusive")
-        if transfer is not None:
-            for side in ("custom", "baseline"):
-                values = transfer[side]["samples_us"]
-                if len(values) != report["samples"] or not all(positive(v) for v in values):
-                    raise ValueError("invalid transfer-inclusive timings")
-                if not math.isclose(transfer[side]["median_us"], statistics.median(values), rel_tol=1e-7):
-                    raise ValueError("transfer median does not match raw samples")
+    found = problems(report)
+    if found:
+        raise EvidenceError(f"{len(found)} problem(s) in the evidence: " + "; ".join(found))
     return report
 
 
 def separated_win(case: dict) -> bool:
-    return case["speedup"] >= 1.05 and max(case["custom"]["samples_us"]) < min(case["baseline"]["samples_us"])
+    return case["speedup"] >= WIN_RATIO and max(case["custom"]["samples_us"]) < min(case["baseline"]["samples_us"])
 
 
-def _p95(xs):
-    xs = sorted(xs)
-    return xs[math.ceil(0.95 * len(xs)) - 1]
+def verdict(case: dict) -> str:
+    if separated_win(case):
+        return "separated win"
+    return "slower" if case["speedup"] < 1 else "inconclusive"
+
+
+def p95(xs) -> float:
+    """Nearest-rank 95th percentile."""
+    ordered = sorted(xs)
+    return ordered[max(0, math.ceil(0.95 * len(ordered)) - 1)]
 
 
 def case_bytes(case: dict) -> int:
     h, i = case["hidden"], case["intermediate"]
-    return intensity.projection(h, i)["bytes"] if case["operation"] == "projection" else intensity.layer(h, i)["bytes"]
+    model = intensity.projection if case["operation"] == "projection" else intensity.layer
+    return model(h, i)["bytes"]
+
+
+def _table(header: list[str], align: str, rows: list[list[str]]) -> list[str]:
+    rule = ["---:" if a == "r" else "---" for a in align]
+    return ["| " + " | ".join(header) + " |", "| " + " | ".join(rule) + " |"] + \
+           ["| " + " | ".join(r) + " |" for r in rows]
 
 
 def render(report: dict, hbm_gbs: float | None = None) -> str:
     validate(report)
     peak = hbm_gbs or report.get("hbm_peak_gbs") or intensity.measured_peaks()["hbm_gbs"]
-    lines = [f"GPU: {report['gpu']} (SM {report.get('compute_capability', '?')}).",
-             f"CUDA runtime {report['runtime_version']}; cuBLAS {report['cublas_version']}."]
-    if report.get("result_class"):
-        lines.append(f"Result class: `{report['result_class']}`.")
-    lines += ["", f"Data: `{report['data']}`. Rotating weight copies larger than L2; warmed CUDA graphs; "
-              "GPU event timing.", "Kernel-only holdout samples follow tuning. Reference checks and tuning are "
-              "excluded from latency.", "",
-              f"| Workload | Operation | Custom µs | cuBLAS µs | Ratio | Evidence | Bytes | Custom GB/s | % of {peak:.0f} GB/s |",
-              "|---|---|---:|---:|---:|---|---:|---:|---:|"]
-    for c in report["cases"]:
-        a, b = c["custom"], c["baseline"]
-        evidence = "separated win" if separated_win(c) else ("slower" if c["speedup"] < 1 else "inconclusive")
+    cases = report["cases"]
+    main_rows = []
+    for c in cases:
         nbytes = case_bytes(c)
-        gbs = nbytes / (a["median_us"] * 1e-6) / 1e9
-        lines.append(f"| {c['shape']} | {c['operation']} | {a['median_us']:.3f} | {b['median_us']:.3f} | "
-                     f"{c['speedup']:.3f}× | {evidence} | {nbytes} | {gbs:.0f} | {100 * gbs / peak:.1f} |")
-    lines += ["", "Tail latency (nearest-rank p95 of replay-batch averages):", "",
-              "| Workload | Operation | Custom p95 µs | Baseline p95 µs |", "|---|---|---:|---:|"]
-    for c in report["cases"]:
-        lines.append(f"| {c['shape']} | {c['operation']} | {_p95(c['custom']['samples_us']):.3f} | "
-                     f"{_p95(c['baseline']['samples_us']):.3f} |")
-    if any("transfer_inclusive" in c for c in report["cases"]):
-        lines += ["", "Transfer-inclusive (pinned H2D of the token input, kernel graph, D2H of the output; "
-                  "weights resident):", "",
-                  "| Workload | Operation | Custom µs | cuBLAS µs | Custom p95 µs | Baseline p95 µs |",
-                  "|---|---|---:|---:|---:|---:|"]
-        for c in report["cases"]:
-            t = c.get("transfer_inclusive")
-            if t:
-                lines.append(f"| {c['shape']} | {c['operation']} | {t['custom']['median_us']:.3f} | "
-                             f"{t['baseline']['median_us']:.3f} | {_p95(t['custom']['samples_us']):.3f} | "
-                             f"{_p95(t['baseline']['samples_us']):.3f} |")
-    lines += ["", "A separated win requires at least 5% median speedup and every custom sample below every "
-              "baseline sample.", "This compares the selected cuBLAS GemmEx algorithms, not cuBLASLt or "
-              "TensorRT-LLM. Synthetic shapes are not pretrained-model evidence."]
-    return "\n".join(lines) + "\n"
+        gbs = nbytes / (c["custom"]["median_us"] * 1e-6) / 1e9
+        main_rows.append([c["shape"], c["operation"], f"{c['custom']['median_us']:.3f}",
+                          f"{c['baseline']['median_us']:.3f}", f"{c['speedup']:.3f}×", verdict(c), str(nbytes),
+                          f"{gbs:.0f}", f"{100 * gbs / peak:.1f}"])
+    tail_rows = [[c["shape"], c["operation"], f"{p95(c['custom']['samples_us']):.3f}",
+                  f"{p95(c['baseline']['samples_us']):.3f}"] for c in cases]
+    text = [f"Evidence from {report['gpu']} (compute capability {report.get('compute_capability', '?')}), "
+            f"CUDA runtime {report['runtime_version']}, cuBLAS {report['cublas_version']}"
+            + (f", result class `{report['result_class']}`." if report.get("result_class") else "."),
+            "",
+            f"Inputs: `{report['data']}`, weights rotated through copies larger than L2. Each candidate is a "
+            f"warmed CUDA graph timed with GPU events, {report['samples']} holdout samples of {report['repeats']} "
+            "replays after tuning; the correctness checks and the tuning itself are not in the times.",
+            ""]
+    text += _table(["Workload", "Operation", "Custom µs", "cuBLAS µs", "Ratio", "Verdict", "Bytes",
+                    "Custom GB/s", f"% of {peak:.0f} GB/s"], "llrrrlrrr", main_rows)
+    text += ["", "95th percentile (nearest rank) of the holdout samples:", ""]
+    text += _table(["Workload", "Operation", "Custom p95 µs", "cuBLAS p95 µs"], "llrr", tail_rows)
+    moved = [c for c in cases if c.get("transfer_inclusive")]
+    if moved:
+        rows = [[c["shape"], c["operation"]] + [f"{c['transfer_inclusive'][s]['median_us']:.3f}" for s in SIDES] +
+                [f"{p95(c['transfer_inclusive'][s]['samples_us']):.3f}" for s in SIDES] for c in moved]
+        text += ["", "Transfer-inclusive (the token input copied in from pinned host memory, the graph, the "
+                 "output copied back; weights stay resident):", ""]
+        text += _table(["Workload", "Operation", "Custom µs", "cuBLAS µs", "Custom p95 µs", "cuBLAS p95 µs"],
+                       "llrrrr", rows)
+    text += ["", f"Verdicts: a separated win needs a median ratio of at least {WIN_RATIO} and the slowest custom "
+             "sample faster than the fastest cuBLAS sample. The baseline is cuBLAS GemmEx with the faster of its "
+             "default algorithms plus two pointwise kernels; synthetic weights say nothing about a trained model."]
+    return "\n".join(text) + "\n"
 
 
-def main():
+def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("input", type=Path)
     p.add_argument("--output", type=Path)
-    p.add_argument("--require-win", action="store_true")
-    p.add_argument("--require-all-wins", action="store_true")
-    a = p.parse_args()
-    report = validate(json.loads(a.input.read_text()))
+    p.add_argument("--require-win", action="store_true", help="fail unless some case is a separated win")
+    p.add_argument("--require-all-wins", action="store_true", help="fail unless every case is a separated win")
+    a = p.parse_args(argv)
+    report = json.loads(a.input.read_text())
     text = render(report)
     if a.output:
         a.output.write_text(text)
     else:
         print(text, end="")
-    if a.require_all_wins and not all(separated_win(c) for c in report["cases"]):
-        raise SystemExit("Not every benchmark has a separated win")
-    if a.require_win and not any(separated_win(c) for c in report["cases"]):
-        raise SystemExit("No separated win measured")
+    wins = [separated_win(c) for c in report["cases"]]
+    if a.require_all_wins and not all(wins):
+        raise SystemExit(f"{wins.count(False)} case(s) without a separated win")
+    if a.require_win and not any(wins):
+        raise SystemExit("no case has a separated win")
 
 
 if __name__ == "__main__":
