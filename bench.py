@@ -15,7 +15,7 @@ twice the 126 MB L2, so every step streams its weights from HBM.
   all-reduce). The NCCL all-reduce path is timed beside it as the baseline.
 
 Steps are captured in CUDA graphs: the timed steps run as graphs that each hold
-one step per rotating weight copy back to back (as the layers of a decode step);
+up to 32 consecutive layer steps (the FFN layers of one decode step);
 the reference's protocol, one step per graph replay, is timed and reported
 beside it (``one_step_graph_us``), and so are the baselines.
 
@@ -56,7 +56,7 @@ def parse():
     p.add_argument("--gate-config", type=int, default=0, help="registry id (0 = tune)")
     p.add_argument("--down-config", type=int, default=0, help="registry id (0 = tune)")
     p.add_argument("--graph-steps", type=int, default=0,
-                   help="layer steps per CUDA graph (0 = one per rotating weight copy, 1 = one step per graph)")
+                   help="layer steps per CUDA graph (0 = a decode step of up to 32 layers, 1 = one step per graph)")
     p.add_argument("--no-prefetch-weights", action="store_true",
                    help="launch each step's gate in plain stream order (no SWB_PREFETCH_WEIGHTS)")
     p.add_argument("--layer-config", type=int, default=0,
@@ -424,11 +424,14 @@ def ours(args) -> None:
 
     # ---- CUDA graphs. One graph per rotating copy holds one whole step (the reference's
     # protocol: src/benchmark.cu:46-83, one captured call replayed); the timed steps are
-    # issued as graphs that each hold `chain` consecutive steps, one per weight copy, as the
-    # layers of a decode step run back to back in one graph. Every step still does all of
-    # its work; `one_step_graph_us` reports the one-step-per-graph protocol beside it.
-    chain = args.graph_steps if args.graph_steps > 0 else copies
-    chain = max(1, min(chain, copies))
+    # issued as graphs that each hold `chain` consecutive layer steps, as the FFN layers of
+    # one decode step run back to back in one graph: up to 32 (the layer count of the
+    # 32-layer model this 4096 -> 14336 FFN belongs to) and at most K, a whole number of
+    # passes over the rotating weight copies, so consecutive steps never share a copy. Every
+    # step does all of its work; `one_step_graph_us` reports the one-step-per-graph protocol.
+    chain = args.graph_steps if args.graph_steps > 0 else min(args.steps, 32)
+    if chain > copies:
+        chain = chain // copies * copies
 
     def capture(fn, first, n):
         g = torch.cuda.CUDAGraph()
@@ -764,7 +767,8 @@ def ours(args) -> None:
                        "parallelism": f"tp{world}", "gate_config": gcfg, "down_config": dcfg,
                        "layer_config": lcfg or None,
                        "prefetch_weights": bool(flags),
-                       "graph": f"{chain} consecutive steps (one per weight copy) per CUDA graph replay"
+                       "graph": f"{chain} consecutive layer steps per CUDA graph replay (a decode step's FFN "
+                                f"layers; weights rotate through {copies} copies)"
                                 if chain > 1 else "one step per CUDA graph replay",
                        "rotating_copies": copies,
                        "l2": f"inputs larger than L2: {copies} rotating weight copies of "

@@ -762,8 +762,11 @@ struct TpParams {
 // everywhere -- plus bias and residual. A rank can run at most one call ahead of
 // a peer (each call waits for that peer's slots), so the parity double buffer
 // keeps a slot from being rewritten before it is read.
-template <int CT, class Own>
-__device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, float* y,
+__device__ __forceinline__ void store_out(float* y, int i, float v) { y[i] = v; }
+__device__ __forceinline__ void store_out(__half* y, int i, float v) { y[i] = __float2half_rn(v); }
+
+template <int CT, class Out, class Own>
+__device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, Out* y,
                                                  Own own) {
     // rank loops run to the compile-time bound, so recv[] is indexed by constants
     // and stays in the kernel's parameter space
@@ -795,7 +798,7 @@ __device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t ep
         float add = 0.f;
         if (tp.bias) add += __half2float(tp.bias[r0 + i]);
         if (tp.residual) add += __half2float(tp.residual[r0 + i]);
-        y[r0 + i] = acc + add;
+        store_out(y, r0 + i, acc + add);
     }
 }
 
@@ -803,7 +806,9 @@ __device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t ep
 // its epilogue (tp_exchange_rows). Every rank runs the same grid and row
 // partition, so CTA b owns rows [r0, r1) of y on every rank. The epoch lives in
 // device memory (advanced by the gate kernel), so graph replays need no reset.
-template <int CW, int MAXJ, int CPS>
+// HALF_OUT writes the reduced rows rounded once to fp16 into p.h (the model
+// path: fp16 y, no bias, no residual); otherwise fp32 into p.y.
+template <int CW, int MAXJ, int CPS, bool HALF_OUT>
 __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(const Params p, const TpParams tp) {
     constexpr int CT = CW * 32;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -812,7 +817,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(con
     float* part;
     if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part, &s_epoch)) return;
     named_barrier_sync(1, CT);
-    tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.y, [&](int i) { return row_sum<CW, 1>(part, i, 0); });
+    auto own = [&](int i) { return row_sum<CW, 1>(part, i, 0); };
+    if constexpr (HALF_OUT)
+        tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.h, own);
+    else
+        tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.y, own);
 }
 
 // ===================================================================== SBULK

@@ -242,7 +242,7 @@ int launch_rbulk(Params p, cudaStream_t stream, bool pdl) {
 // The fused tensor-parallel down projection (rbulk_allreduce_kernel). Every rank
 // must launch the same grid: the plan depends only on the shape, the geometry
 // and the SM count, which match across ranks of one machine.
-template <int CW, int CPS, int MAXJ, int STAGE_BYTES, int ST>
+template <int CW, int CPS, int MAXJ, int STAGE_BYTES, int ST, bool HALF>
 int launch_rbulk_ar(Params p, const TpParams& tp, cudaStream_t stream, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
     const int nv = p.cols / 8;
@@ -269,7 +269,7 @@ int launch_rbulk_ar(Params p, const TpParams& tp, cudaStream_t stream, bool pdl)
     p.stages = stages;
     p.row_stage = rs;
     const size_t smem = rbulk_layout(1, rs, p.cols, stages, CW, rows_per_cta).total;
-    auto kernel = rbulk_allreduce_kernel<CW, MAXJ, CPS>;
+    auto kernel = rbulk_allreduce_kernel<CW, MAXJ, CPS, HALF>;
     if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
     if (!pdl) {
         kernel<<<unsigned(G), (CW + 1) * 32, smem, stream>>>(p, tp);
@@ -295,8 +295,9 @@ struct Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST> {
     static int run(Params p, cudaStream_t s, bool pdl) {
         return launch_rbulk<W, R, U, CH, ST, MODE>(p, s, pdl);
     }
-    static int run_allreduce(const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
-        return launch_rbulk_ar<W, R, U, CH, ST>(p, tp, s, pdl);
+    static int run_allreduce(const Params& p, const TpParams& tp, cudaStream_t s, bool pdl, bool half) {
+        return half ? launch_rbulk_ar<W, R, U, CH, ST, true>(p, tp, s, pdl)
+                    : launch_rbulk_ar<W, R, U, CH, ST, false>(p, tp, s, pdl);
     }
 };
 
@@ -350,7 +351,7 @@ struct Launcher<SWB_FAM_SBULK, W, R, PK, U, CH, ST> {
 template <int FAM>
 struct AllreduceDispatch {
     template <int W, int R, int PK, int U, int CH, int ST>
-    static int run(const Params&, const TpParams&, cudaStream_t, bool) {
+    static int run(const Params&, const TpParams&, cudaStream_t, bool, bool) {
         return fail(SWB_E_CONFIG_INVALID, "the fused tensor-parallel path needs an RBULK geometry");
     }
 };
@@ -358,33 +359,34 @@ struct AllreduceDispatch {
 template <>
 struct AllreduceDispatch<SWB_FAM_RBULK> {
     template <int W, int R, int PK, int U, int CH, int ST>
-    static int run(const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
-        return Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST>::run_allreduce(p, tp, s, pdl);
+    static int run(const Params& p, const TpParams& tp, cudaStream_t s, bool pdl, bool half) {
+        return Launcher<SWB_FAM_RBULK, W, R, PK, U, CH, ST>::run_allreduce(p, tp, s, pdl, half);
     }
 };
 
-int dispatch_allreduce_one(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl);
+int dispatch_allreduce_one(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl, bool half);
 
 // RBULK geometries tried, in order, when the requested one cannot hold a row of
 // the shape (the fused epilogue exists only in the RBULK kernel).
 constexpr int kAllreduceFallbacks[] = {87, 85, 82};
 
-int dispatch_allreduce(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
-    int rc = dispatch_allreduce_one(id, p, tp, s, pdl);
+// half: fp16 rows into p.h (the model path) instead of fp32 into p.y.
+int dispatch_allreduce(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl, bool half = false) {
+    int rc = dispatch_allreduce_one(id, p, tp, s, pdl, half);
     if (rc != SWB_E_UNSUPPORTED) return rc;
     for (int alt : kAllreduceFallbacks) {
         if (alt == id) continue;
-        rc = dispatch_allreduce_one(alt, p, tp, s, pdl);
+        rc = dispatch_allreduce_one(alt, p, tp, s, pdl, half);
         if (rc != SWB_E_UNSUPPORTED) return rc;
     }
     return rc;
 }
 
-int dispatch_allreduce_one(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl) {
+int dispatch_allreduce_one(int64_t id, const Params& p, const TpParams& tp, cudaStream_t s, bool pdl, bool half) {
     switch (id) {
 #define SWB_AR_CASE(ID, FAM, W, R, PK, U, CH, ST) \
     case ID:                                      \
-        return AllreduceDispatch<FAM>::template run<W, R, PK, U, CH, ST>(p, tp, s, pdl);
+        return AllreduceDispatch<FAM>::template run<W, R, PK, U, CH, ST>(p, tp, s, pdl, half);
         SWB_CONFIGS(SWB_AR_CASE)
 #undef SWB_AR_CASE
         default:
@@ -913,6 +915,44 @@ int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const vo
     p.cols = shard;
     p.epoch = t.ctr;
     return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true);
+}
+
+int swb_swiglu_tp_out(swb_tp_t* tp, const void* x, const void* gate_shard, const void* up_shard,
+                      const void* down_shard, void* h_shard, void* y, int64_t hidden, int64_t shard,
+                      int64_t gate_config, int64_t down_config, unsigned flags, void* stream) {
+    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
+    if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != tp->device)
+        return fail(SWB_E_INPUT, "the current device is not the exchange's device");
+    // the binding's guards, in its order (src/torch_extension.cu:17-30), on the rank's shard
+    if (!(hidden > 0 && shard > 0 && hidden <= 100000 && shard <= 100000)) return fail(SWB_E_SHAPE);
+    if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
+    if (!(gate_config >= 0 && gate_config <= 1000 && down_config >= 0 && down_config <= 1000))
+        return fail(SWB_E_CONFIG_RANGE);
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG_INVALID);
+    if (!x || !gate_shard || !down_shard) return fail(SWB_E_INPUT);
+    if (!up_shard || !h_shard) return fail(SWB_E_GATE_BUFFERS);
+    if (!y) return fail(SWB_E_HALF_OUTPUT);
+    const size_t hb = size_t(hidden) * 2, sb = size_t(shard) * 2, wb = size_t(hidden) * size_t(shard) * 2;
+    const void* inputs[4] = {x, gate_shard, up_shard, down_shard};
+    const size_t sizes[4] = {hb, wb, wb, wb};
+    for (int i = 0; i < 4; ++i)
+        if (overlaps(h_shard, sb, inputs[i], sizes[i]) || overlaps(y, hb, inputs[i], sizes[i]))
+            return fail(SWB_E_OVERLAP_INPUT);
+    if (overlaps(h_shard, sb, y, hb)) return fail(SWB_E_OVERLAP_OUTPUT);
+    const TpParams t = tp_params(tp, nullptr, nullptr);  // no bias, no residual: the model adds its own
+    if (int rc = gate_impl(int(gate_config), gate_shard, up_shard, x, nullptr, nullptr, h_shard, int(shard),
+                           int(hidden), 1, stream, t.ctr, (flags & SWB_PREFETCH_WEIGHTS) != 0))
+        return rc;
+    Params p = make_params();
+    p.w = static_cast<const __half*>(down_shard);
+    p.x = static_cast<const __half*>(h_shard);
+    p.h = static_cast<__half*>(y);
+    p.rows = int(hidden);
+    p.cols = int(shard);
+    p.epoch = t.ctr;
+    return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true, true);
 }
 
 }  // extern "C"

@@ -93,6 +93,12 @@ def problems(data: dict) -> list[str]:
         return out + ["no cases"]
     for c in cases:
         out += _case_problems(c, layers)
+        if isinstance(c, dict) and c.get("eager") is not None:  # the runner's eager decodes, same rules
+            e = dict(c["eager"], prompt=f"{c.get('prompt', '?')} (eager)", tokens=c.get("tokens"),
+                     exact_greedy_match=c.get("exact_greedy_match"), logits_close=c.get("logits_close"),
+                     max_logit_abs_error=c.get("max_logit_abs_error"),
+                     max_logit_scaled_error=c.get("max_logit_scaled_error"))
+            out += _case_problems(e, layers)
     return out
 
 
@@ -111,8 +117,9 @@ def render(data: dict) -> str:
     extra = [f"{k} {data[k]}" for k in ("ranks", "decode") if data.get(k)]
     lines = [f"`{data['model']}` (revision `{data['resolved_revision']}`) on {data['gpu']}: fp16, batch 1, "
              f"{data['patched_layers']} decode MLPs replaced" + (f", {', '.join(extra)}" if extra else "") + ".",
-             "Both paths prefill with the stock model and decode on the same growing KV cache; prefill and "
-             "set-up are not timed.", "",
+             "Both sides prefill with the stock model and decode the same way ("
+             + (data.get("decode") or "the transformers loop on its growing KV cache")
+             + "); prefill, capture and set-up are not timed.", "",
              "| Prompt | Stock ms/token | Custom ms/token | Stock GPU ms | Custom GPU ms | Wall ratio | Verdict |",
              "|---|---:|---:|---:|---:|---:|---|"]
     for c in data["cases"]:
@@ -120,6 +127,16 @@ def render(data: dict) -> str:
         b, k = c["baseline"], c["custom"]
         lines.append(f"| {prompt} | {b['wall_median_ms']:.3f} | {k['wall_median_ms']:.3f} | {b['gpu_median_ms']:.3f} | "
                      f"{k['gpu_median_ms']:.3f} | {c['wall_speedup']:.3f}× | {verdict(c)} |")
+    eager = [c for c in data["cases"] if c.get("eager")]
+    if eager:
+        lines += ["", "The same prompts through the transformers decode loop (one Python call per kernel, growing "
+                  "cache), stock MLPs against replaced ones:", "",
+                  "| Prompt | Stock ms/token | Custom ms/token | Wall ratio | Verdict |", "|---|---:|---:|---:|---|"]
+        for c in eager:
+            e = c["eager"]
+            prompt = str(c["prompt"]).replace("|", "\\|").replace("\n", " ")[:55]
+            lines.append(f"| {prompt} | {e['baseline']['wall_median_ms']:.3f} | {e['custom']['wall_median_ms']:.3f} | "
+                         f"{e['wall_speedup']:.3f}× | {verdict(e)} |")
     lines += ["", "Accepted only with identical greedy tokens, logits within the runner's tolerance and every "
               "timed decode MLP on the replaced path. At model level attention, the KV cache and the host loop "
               "share the time with the MLPs, so a kernel win shrinks."]

@@ -107,3 +107,17 @@ def ffn_tp_fused(ex: Exchange, x: torch.Tensor, s: dict, bd: torch.Tensor | None
                                                   s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
                                                   x.data_ptr(), ptr(s["bg"]), ptr(s["bu"]), ptr(bd), h.data_ptr(),
                                                   y.data_ptr(), hidden, shard_rows, flags, sp))
+
+
+def swiglu_tp_out(ex: Exchange, x: torch.Tensor, s: dict, h: torch.Tensor, y: torch.Tensor, gate_config: int,
+                  down_config: int, stream: int | None = None, prefetch_weights: bool = False) -> None:
+    """``swiglu_out`` for one tensor-parallel rank (the model path): eager-fp16 rounding in the
+    gate on the rank's shard, the fused down projection + exchange, y = fp16 of the ranks' summed
+    partials (no bias, no residual), identical on every rank. x, y: [..., hidden] fp16; h: [shard]."""
+    shard_rows, hidden = s["wg"].shape
+    sp = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+    flags = _lib.SWB_PREFETCH_WEIGHTS if prefetch_weights else 0
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().swb_swiglu_tp_out(ex.handle, x.data_ptr(), s["wg"].data_ptr(), s["wu"].data_ptr(),
+                                                s["wd"].data_ptr(), h.data_ptr(), y.data_ptr(), hidden, shard_rows,
+                                                int(gate_config), int(down_config), flags, sp))

@@ -193,6 +193,19 @@ SWB_API int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, con
                              const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,
                              void* stream);
 
+/* swiglu_out (src/torch_extension.cu:7-40) for one tensor-parallel rank: the
+ * binding's shape / config / alias guards on the rank's shard, the model-rounding
+ * gate on gate_shard, up_shard ([shard, hidden]) into h_shard [shard], then the
+ * fused down projection of down_shard ([hidden, shard]) + exchange; y [hidden] fp16
+ * = fp16(sum over ranks of the fp32 partials, added in rank order), identical on
+ * every rank, with no bias and no residual (the transformer layer adds its own).
+ * Every rank makes the same calls with the same geometries; down_config is an
+ * RBULK id (87, 85 or 82 run when its rows cannot hold the shard). flags:
+ * SWB_PREFETCH_WEIGHTS or 0. */
+SWB_API int swb_swiglu_tp_out(swb_tp_t* tp, const void* x, const void* gate_shard, const void* up_shard,
+                              const void* down_shard, void* h_shard, void* y, int64_t hidden, int64_t shard,
+                              int64_t gate_config, int64_t down_config, unsigned flags, void* stream);
+
 /* swb_ffn and swb_ffn_tp_fused with launch flags (no counterpart in the reference).
  * SWB_PREFETCH_WEIGHTS: the gate kernel is launched programmatically as well, so
  * its stream of Wg/Wu may begin while the kernel before it in the stream is still

@@ -1,9 +1,12 @@
-"""TinyLlama-architecture decode with every decode MLP on the B200 kernels.
+"""TinyLlama-architecture decode with every decode MLP on the B200 kernels, one GPU.
 
-The gates of tools/model_bench.py:141-147: every decode MLP call took the custom
-path (calls == tokens x layers), logits within atol .1 / rtol .02 of the stock
-fp16 path, and greedy tokens identical. Random init (seed 0) and seeded token-id
-prompts of length 16, 32 and 64 stand in for the pretrained model and its prompts.
+The gates of tools/model_bench.py:141-147, for four decodes of each of three seeded
+prompts (16, 32, 64 token ids; random init, seed 0): the transformers loop with stock
+and with replaced MLPs, and one CUDA graph per decode step with stock and with
+replaced MLPs. Greedy tokens identical to the eager stock decode, logits within atol .1 /
+rtol .02, every replaced decode routed through tokens x layers kernel calls; the graph
+decode with stock MLPs reproduces the eager stock logits bit for bit (the slot cache
+gives attention the shapes the growing cache gives it).
 """
 import pytest
 import torch
@@ -11,22 +14,18 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def test_tinyllama_architecture_greedy_decode_identical():
-    from swiglu_b200 import model_runner, model_report
-    ids = [16, 33, 64, 69, 80, 87]
-    pairs = [(g, d) for g in ids for d in ids]
-    model = model_runner.build_model(seed=0, layers=22)
-    import decode_swiglu as ext
-    patched = model_runner.PatchedMLPs(model, ext)
-    best, tuning = model_runner.tune_layer0(model, patched, ext, samples=3, replays=20, pairs=pairs)
-    assert len(tuning) == len(pairs)
-    del model, patched
-    torch.cuda.empty_cache()
-    result = model_runner.run(tokens=32, samples=3, layers=22, seed=0,
-                              pair=(best["gate_config"], best["down_config"]))
-    assert result["patched_layers"] == 22
+def test_tinyllama_architecture_greedy_decode_eager_and_graph():
+    from swiglu_b200 import model_report, model_runner
+    ids = [16, 33, 69, 80, 87, 96]
+    cands = [(g, d) for g in ids for d in ids]
+    result = model_runner.run(tokens=32, samples=3, layers=22, seed=0, candidates=cands)
+    assert result["patched_layers"] == 22 and len(result["tuning"]) == len(cands)
     for case in result["cases"]:
         assert case["exact_greedy_match"] and case["logits_close"]
         assert all(s["calls"] == 32 * 22 for s in case["custom"]["samples"])
-    text = model_report.render(result)  # re-validates routing, medians and the speedup
+        assert all(s["calls"] == 32 * 22 for s in case["eager"]["custom"]["samples"])
+        assert all(c["tokens_equal"] for c in case["checks"].values())
+        assert case["checks"]["graph_stock"]["bit_identical_logits"]
+    text = model_report.render(result)  # re-validates routing, medians and the speedups
     assert "random-init-seed-0" in text
+    torch.cuda.empty_cache()

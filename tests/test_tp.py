@@ -209,6 +209,44 @@ def test_fused_tp_prefetch_chain_matches_plain(gcfg):
 
 
 @pytest.mark.gpu
+def test_model_path_rank_matches_swiglu_out_and_oracle():
+    """swb_swiglu_tp_out on a one-rank exchange is the binding's swiglu_out (model rounding,
+    fp16 y, no bias or residual) with the down projection's rows summed through the exchange:
+    bit-identical to swiglu_out with the same geometries, within the binding's tolerance of
+    the oracle's fp16 pipeline; its guards reject what swiglu_out rejects."""
+    from swiglu_b200 import binding
+    from swiglu_b200 import tp as T
+    H, I = 2048, 5632
+    w = O.normal_workload(4, H, I)
+    h_ref, y_ref = O.ffn_model(w)
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    s = {"wg": t(w["wg"]), "wu": t(w["wu"]), "wd": t(w["wd"])}
+    x = t(w["x"]).view(1, 1, H)
+    h, h1 = torch.empty(I, dtype=torch.float16, device=dev), torch.empty(I, dtype=torch.float16, device=dev)
+    y, y1 = torch.empty_like(x), torch.empty_like(x)
+    ex = T.Exchange(0, 1, H, dev)
+    for g, d in ((69, 87), (33, 85), (96, 82), (79, 80)):
+        binding.swiglu_out(x, s["wg"], s["wu"], s["wd"], h1, y1, g, d)
+        T.swiglu_tp_out(ex, x, s, h, y, g, d)
+        torch.cuda.synchronize()
+        assert torch.equal(h, h1) and torch.equal(y, y1), (g, d)
+        yc = y.cpu().numpy().ravel().astype(np.float64)
+        e = y_ref.astype(np.float64)
+        assert np.max(np.abs(yc - e) / (np.abs(e) + 1e-3 * np.abs(e).max())) <= 1e-2
+    with pytest.raises(RuntimeError, match="workspace overlaps input storage"):
+        T.swiglu_tp_out(ex, x, s, h, x, 69, 87)
+    with pytest.raises(RuntimeError, match="configuration out of range"):
+        T.swiglu_tp_out(ex, x, s, h, y, 1001, 87)
+    with pytest.raises(RuntimeError, match="invalid configuration"):
+        T.swiglu_tp_out(ex, x, s, h, y, 69, 999)
+    with pytest.raises(RuntimeError, match="RBULK"):
+        T.swiglu_tp_out(ex, x, s, h, y, 69, 33)
+    assert binding.device_error() == 0
+    ex.close()
+
+
+@pytest.mark.gpu
 def test_every_call_advances_the_exchange_epoch_once():
     """Each fused tensor-parallel call advances the exchange's call epoch exactly once,
     whichever gate family runs it. Under work stealing (SBULK ids) the CTA that owns row 0

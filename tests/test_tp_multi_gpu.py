@@ -100,6 +100,14 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
         g.reset()
     torch.cuda.synchronize()
     assert all(torch.equal(yk, plain) for yk in chain_ys)
+    # the model path (swiglu_out of a rank: model-rounding gate, fp16 y summed over the ranks)
+    s_model = {"wg": wg, "wu": wu, "wd": wd}
+    xm = x.view(1, 1, hidden)
+    ym = torch.empty_like(xm)
+    for gate, down in ((69, 87), (96, 80)):
+        T.swiglu_tp_out(ex, xm, s_model, h, ym, gate, down)
+        torch.cuda.synchronize()
+        q.put((rank, ("model", gate, down, ym.cpu().numpy().ravel().copy())))
     # every call advanced the exchange's epoch once on every rank, whichever gate ran it
     # (SBULK work stealing included): 100 back-to-back calls, no host synchronisation
     before = ex.epoch()
@@ -128,11 +136,14 @@ def test_tp_nccl_matches_oracle(world):
     procs = [ctx.Process(target=_rank, args=(r, world, port, hidden, inter, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = {}
-    for _ in range(world):
+    results, model = {}, {}
+    while len(results) < world:
         rank, out = q.get(timeout=300)
         assert not isinstance(out, str), out
-        results[rank] = out
+        if isinstance(out, tuple) and out[0] == "model":
+            model.setdefault(rank, []).append(out[1:])
+        else:
+            results[rank] = out
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -146,3 +157,11 @@ def test_tp_nccl_matches_oracle(world):
     for rank in range(1, world):
         for y0, yr in zip(results[0], results[rank]):
             assert np.array_equal(y0, yr)  # every rank holds the same reduced y
+    # model path: fp16 y against the oracle's eager-fp16 pipeline at the binding's tolerance
+    _, ym_ref = O.ffn_model(w)
+    e = ym_ref.astype(np.float64)
+    for rank in range(world):
+        assert len(model[rank]) == 2
+        for (g, d, ym), (_, _, ym0) in zip(model[rank], model[0]):
+            assert np.max(np.abs(ym.astype(np.float64) - e) / (np.abs(e) + 1e-3 * np.abs(e).max())) <= 1e-2, (g, d)
+            assert np.array_equal(ym.view(np.uint16), ym0.view(np.uint16))
