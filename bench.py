@@ -322,9 +322,9 @@ def ours(args) -> None:
         # (and, for N > 1, the exchange) in one persistent kernel
         s = sets[i % copies]
         if world == 1 and cfg:
-            _lib.check(L.swb_ffn_fused(cfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
-                                       x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
-                                       y.data_ptr(), H, shard, workspace.data_ptr(), sp))
+            _lib.check(L.swb_ffn_fused_ex(cfg, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                          x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
+                                          y.data_ptr(), H, shard, workspace.data_ptr(), flags, sp))
         elif world == 1:
             _lib.check(L.swb_ffn_ex(g, d, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
                                     x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),

@@ -28,10 +28,11 @@ struct LayerParams {
     const __half* bd;
     __half* h;
     float* y;
-    uint32_t* sync;  // [0]: grid-barrier word (zero before the first call; see layer_kernel)
+    uint32_t* sync;  // [0]: grid-barrier word (zero before the first call; see layer_kernel);
+                     // stream_layer_kernel: [1] CTAs done, [kStreamCountBase + c] rows of h block c
     int hidden;      // phase 1: inter rows x hidden cols; phase 2: hidden rows x inter cols
     int inter;
-    int rs1, rs2;    // whole rows per ring stage in each phase
+    int rs1, rs2;    // whole rows per ring stage in each phase (stream_layer_kernel: rs1 only)
     int stages;
     int stage_bytes;
 };
@@ -269,6 +270,311 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
             for (int j = 0; j < CW; ++j) a += part2[size_t(i) * CW + j];
             return a;
         });
+    }
+}
+
+
+// ====================================================== streaming whole layer
+//
+// stream_layer_kernel (layer ids 220+): the whole layer in one persistent kernel
+// with no grid barrier. Phase 1 gives CTA b the gate rows b, b + G, b + 2G, ... so
+// that the grid writes h in ascending order; the last consumer warp to finish a
+// ring stage writes that stage's h rows and counts them, with release semantics,
+// in the word of their column block (CB = 8 * CT / RSPLIT elements of h). Phase 2
+// gives CTA b the contiguous rows [d0, d1) of y and streams them block by block:
+// a stage holds the block's CB columns of each of the CTA's rows, and the
+// consumers read it as soon as the block's word says that all its h elements are
+// written (acquire, bounded wait). A CTA therefore waits only for the blocks the
+// slowest CTAs are still producing, while it streams and multiplies the others;
+// the one producer thread never stops: Wg/Wu rows, then Wd blocks, through one
+// ring. Consumer thread t owns vector t mod (CT / RSPLIT) of a block and rows
+// t div (CT / RSPLIT) + RSPLIT * i, accumulating each row in a register across
+// blocks; at the end each row is reduced over its threads in a fixed order, so
+// the result is deterministic. The last CTA to finish resets the block words (and,
+// tensor parallel, advances the exchange epoch every CTA read at its start), so
+// calls need no clearing; after a device error zero the words again. Launched
+// cooperatively, or programmatically after the kernel before it in the stream
+// (SWB_PREFETCH_WEIGHTS): then the grid is no larger than what fits at once, and
+// a CTA that is not yet resident only makes the others wait.
+constexpr int kLayerWorkspaceWords = 2048;  // SWB_LAYER_WORKSPACE_BYTES / 4
+constexpr int kStreamCountBase = 64;       // first block word in LayerParams::sync
+constexpr int kStreamMaxBlocks = kLayerWorkspaceWords - kStreamCountBase;
+
+struct StreamLayout {
+    size_t ring, full, empty, cnt, bias, part1, part2, total;
+};
+
+// rpc1 / rpc2: most gate rows / y rows of one CTA.
+__host__ __device__ inline StreamLayout stream_layout(int stage_bytes, int stages, int cw, int rpc1, int rpc2) {
+    StreamLayout Y;
+    Y.ring = 0;
+    Y.full = align_up(size_t(stages) * stage_bytes, 16);
+    Y.empty = Y.full + size_t(stages) * 8;
+    Y.cnt = Y.empty + size_t(stages) * 8;                         // consumer warps done per stage
+    Y.bias = align_up(Y.cnt + size_t(stages) * 4, 16);            // [row][bg, bu] of the CTA's gate rows
+    Y.part1 = align_up(Y.bias + size_t(rpc1) * 2 * 4, 16);        // [row][warp][gate, up]
+    Y.part2 = align_up(Y.part1 + size_t(rpc1) * cw * 2 * 4, 16);  // [row][warp]
+    Y.total = align_up(Y.part2 + size_t(rpc2) * cw * 4, 16);
+    return Y;
+}
+
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits (bounded) until *p >= target. On time-out records SWB_DEVERR_TIMEOUT, returns false.
+__device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_gpu(p) < target) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_device_error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+
+template <int CW, int CPS, int RSPLIT, int MAXR, bool TP>
+__global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const LayerParams L, const TpParams tp) {
+    constexpr int CT = CW * 32;
+    constexpr int VPB = CT / RSPLIT;  // 16-byte vectors of a block row = threads per row slot
+    constexpr int CB = VPB * 8;       // h elements (Wd columns) per block
+    static_assert(VPB % 32 == 0, "a row slot is whole warps");
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ int s_failed;
+
+    const int G = gridDim.x, b = blockIdx.x;
+    const int H = L.hidden, I = L.inter;
+    const int nA = b < I ? (I - b + G - 1) / G : 0;  // gate rows b + k G, k < nA
+    const int d0 = int((long long)b * H / G), d1 = int((long long)(b + 1) * H / G);
+    const int nD = d1 - d0;
+    const int rs1 = L.rs1;
+    const int units1 = (nA + rs1 - 1) / rs1;
+    const int nblk = (I + CB - 1) / CB;
+    const int rpc1 = (I + G - 1) / G, rpc2 = (H + G - 1) / G;
+    const int stages = L.stages;
+    const StreamLayout Y = stream_layout(L.stage_bytes, stages, CW, rpc1, rpc2);
+    unsigned char* ring = smem + Y.ring;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Y.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + Y.empty);
+    int* done_cnt = reinterpret_cast<int*>(smem + Y.cnt);
+    float* sbias = reinterpret_cast<float*>(smem + Y.bias);
+    float* part1 = reinterpret_cast<float*>(smem + Y.part1);
+    float* part2 = reinterpret_cast<float*>(smem + Y.part2);
+    uint32_t* blk = L.sync + kStreamCountBase;
+    uint32_t* ctas_done = L.sync + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        s_failed = 0;
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), CW);
+            done_cnt[s] = 0;
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    griddep_launch_dependents();
+
+    if (warp == CW) {
+        // ------------------------------------------------------- producer
+        if (lane != 0) return;
+        const uint64_t pol = l2_evict_first_policy();
+        int s = 0, issued = 0;
+        uint32_t ph = 0;
+        for (int k = 0; k < units1 + nblk; ++k) {
+            if (k >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) break;
+            const uint32_t fb = smem_u32(full + s);
+            unsigned char* dst = ring + size_t(s) * L.stage_bytes;
+            if (k < units1) {  // gate rows b + (k rs1 + i) G, i < ru: Wg at [i], Wu at [rs1 + i]
+                const int ru = min(rs1, nA - k * rs1);
+                const uint32_t bytes = uint32_t(H) * 2u;
+                mbar_arrive_expect_tx(fb, 2u * uint32_t(ru) * bytes);
+                for (int i = 0; i < ru; ++i) {
+                    const size_t goff = size_t(b + (k * rs1 + i) * G) * H;
+                    bulk_copy_g2s(smem_u32(dst + size_t(i) * bytes), L.wg + goff, bytes, fb, pol);
+                    bulk_copy_g2s(smem_u32(dst + size_t(rs1 + i) * bytes), L.wu + goff, bytes, fb, pol);
+                }
+            } else {  // columns [c CB, c CB + seg) of rows d0 .. d1 - 1 of Wd, row r at [r CB]
+                const int c0 = (k - units1) * CB;
+                const uint32_t seg = uint32_t(min(CB, I - c0)) * 2u;
+                mbar_arrive_expect_tx(fb, uint32_t(nD) * seg);
+                for (int r = 0; r < nD; ++r)
+                    bulk_copy_g2s(smem_u32(dst + size_t(r) * CB * 2), L.wd + size_t(d0 + r) * I + c0, seg, fb, pol);
+            }
+            ++issued;
+            if (++s == stages) { s = 0; ph ^= 1u; }
+        }
+        const int drain = issued < stages ? issued : stages;
+        for (int j = 1; j <= drain; ++j) {
+            const int k = issued - j;
+            if (!mbar_wait(smem_u32(full + (k % stages)), uint32_t((k / stages) & 1))) break;
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    const int t = threadIdx.x;
+    for (int k = t; k < nA; k += CT) {  // biases do not depend on the previous kernel
+        const int row = b + k * G;
+        sbias[2 * k] = L.bg ? __half2float(L.bg[row]) : 0.f;
+        sbias[2 * k + 1] = L.bu ? __half2float(L.bu[row]) : 0.f;
+    }
+    griddep_wait();  // x may be the previous kernel's output
+    const uint32_t xe = TP ? *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u : 0u;  // this call's epoch
+    named_barrier_sync(1, CT);
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+
+    // ---- phase 1: gate rows b + k G. Lane 0 of the last warp to finish a stage writes the
+    // stage's h rows; it counts them in their blocks' words one stage later (a fence, then
+    // relaxed adds), once those stores have long reached L2, so the fence does not hold it.
+    {
+        float xr[kLayerMaxJ][8];
+        load_slice<CT>(L.x, H, t, false, xr);
+        const int nv = H / 8;
+        int pend_blk = -1, pend_n = 0, pend_blk2 = -1, pend_n2 = 0;  // rows owed to block words (lane 0)
+        auto flush = [&]() {  // lane 0 wrote the h rows it counts here
+            if (lane == 0 && pend_n + pend_n2 > 0) {
+                __threadfence();
+                if (pend_n) atomicAdd(blk + pend_blk, uint32_t(pend_n));
+                if (pend_n2) atomicAdd(blk + pend_blk2, uint32_t(pend_n2));
+            }
+            pend_n = pend_n2 = 0;
+        };
+        auto gate = [&](auto rg, auto jv) {
+            constexpr int RG = decltype(rg)::value, J = decltype(jv)::value;
+            for (int k = 0; k < units1; ++k) {
+                if (!mbar_wait(smem_u32(full + s), ph)) { ok = false; break; }
+                const int ru = min(rs1, nA - k * rs1);
+                const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
+                stage_rows<CW, kLayerMaxJ, 2, RG, J>(sw, ru, rs1, H, nv, xr, part1, k * rs1);
+                __syncwarp();
+                int done = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    done = atomicAdd(done_cnt + s, 1);
+                    mbar_arrive(smem_u32(empty + s));
+                }
+                done = __shfl_sync(0xffffffffu, done, 0);
+                flush();  // what this warp owes from an earlier stage
+                if (done % CW == CW - 1 && lane == 0) {  // the stage's last warp: its h rows
+                    __threadfence_block();
+                    const int first = (b + k * rs1 * G) / CB;
+                    int n1 = 0;
+                    for (int i = 0; i < ru; ++i) {
+                        const int kk = k * rs1 + i, row = b + kk * G;
+                        float ga = sbias[2 * kk], ub = sbias[2 * kk + 1];
+                        for (int j = 0; j < CW; ++j) {
+                            ga += part1[(size_t(kk) * CW + j) * 2];
+                            ub += part1[(size_t(kk) * CW + j) * 2 + 1];
+                        }
+                        L.h[row] = __float2half_rn(silu(ga) * ub);
+                        n1 += row / CB == first;
+                    }
+                    // the stage's rows lie in at most two consecutive blocks ((rs1 - 1) G < CB)
+                    pend_blk = first;
+                    pend_n = n1;
+                    pend_blk2 = first + 1;
+                    pend_n2 = ru - n1;
+                }
+                if (++s == stages) { s = 0; ph ^= 1u; }
+            }
+            flush();
+        };
+        using I1 = std::integral_constant<int, 1>;
+        using I2 = std::integral_constant<int, 2>;
+        using I4 = std::integral_constant<int, 4>;
+        using IJ = std::integral_constant<int, kLayerMaxJ>;
+        const int jn = (nv + CT - 1) / CT;
+        if (jn <= 1) gate(I4{}, I1{});
+        else if (jn <= 2) gate(I2{}, I2{});
+        else gate(I1{}, IJ{});
+    }
+
+    // ---- phase 2: rows [d0, d1) of Wd, block by block as h fills
+    const int slot = t / VPB, v = t % VPB;
+    float acc[MAXR];
+#pragma unroll
+    for (int i = 0; i < MAXR; ++i) acc[i] = 0.f;
+    for (int c = 0; ok && c < nblk; ++c) {
+        if (!mbar_wait(smem_u32(full + s), ph)) { ok = false; break; }
+        const int c0 = c * CB;
+        const int seg = min(CB, I - c0);
+        // every lane acquires the block's word itself before it reads the block's h
+        if (!__all_sync(0xffffffffu, wait_at_least(blk + c, uint32_t(seg)))) { ok = false; break; }
+        if (v * 8 < seg) {
+            float hf[8];
+            const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(L.h + c0) + v);
+            const uint32_t w4[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = half2_bits_to_float2(w4[q]);
+                hf[2 * q] = f.x;
+                hf[2 * q + 1] = f.y;
+            }
+            const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
+#pragma unroll
+            for (int i = 0; i < MAXR; ++i) {
+                const int r = slot + RSPLIT * i;
+                if (r < nD) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(sw + size_t(r) * CB + size_t(v) * 8);
+                    const uint32_t u4[4] = {wv.x, wv.y, wv.z, wv.w};
+                    float a = acc[i];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 f = half2_bits_to_float2(u4[q]);
+                        a = fmaf(f.x, hf[2 * q], a);
+                        a = fmaf(f.y, hf[2 * q + 1], a);
+                    }
+                    acc[i] = a;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        if (++s == stages) { s = 0; ph ^= 1u; }
+    }
+    if (!ok) s_failed = 1;
+    // each row over its slot's VPB threads: warp sums, then the slot's warps in order
+#pragma unroll
+    for (int i = 0; i < MAXR; ++i) {
+        const float a = warp_sum(acc[i]);
+        const int r = slot + RSPLIT * i;
+        if (lane == 0 && r < nD) part2[size_t(r) * CW + (v >> 5)] = a;
+    }
+    named_barrier_sync(1, CT);
+    if (!s_failed) {
+        auto row = [&](int i) {
+            float a = 0.f;
+            for (int j = 0; j < VPB / 32; ++j) a += part2[size_t(i) * CW + j];
+            return a;
+        };
+        if constexpr (!TP) {
+            for (int i = t; i < nD; i += CT) {
+                float a = row(i);
+                if (L.bd) a += __half2float(L.bd[d0 + i]);
+                a += __half2float(L.x[d0 + i]);
+                L.y[d0 + i] = a;
+            }
+        } else {
+            tp_exchange_rows<CT>(tp, xe, H, d0, nD, L.y, row);
+        }
+    }
+    // The last CTA to get here resets the block words (every CTA has passed its waits)
+    // and, tensor parallel, advances the exchange epoch every CTA read at its start.
+    named_barrier_sync(1, CT);
+    if (t == 0) {
+        __threadfence();
+        if (atomicAdd(ctas_done, 1u) == uint32_t(G - 1)) {
+            for (int c = 0; c < nblk; ++c) blk[c] = 0u;
+            *ctas_done = 0u;
+            if (TP) *reinterpret_cast<volatile uint32_t*>(tp.ctr) = xe;
+            __threadfence();
+        }
     }
 }
 

@@ -102,3 +102,16 @@
     X(208, 8, 1, 49152, 4)      \
     X(209, 8, 2, 49152, 2)      \
     X(210, 16, 1, 49152, 4)
+
+// Streaming whole-layer kernels (layer.cuh stream_layer_kernel), layer ids 220+: no grid
+// barrier; the down phase streams Wd block by block as the gate fills h. X(id, consumer
+// warps, CTAs per SM, RSPLIT (row slots: a block is 8 * 32 * warps / RSPLIT h elements),
+// MAXR (rows per thread, so rows per CTA <= RSPLIT * MAXR), target bytes per gate stage,
+// maximum ring depth).
+#define SWB_STREAM_LAYER_CONFIGS(X)     \
+    X(220, 8, 2, 2, 8, 32768, 4)         \
+    X(221, 8, 1, 2, 16, 32768, 6)        \
+    X(222, 16, 1, 4, 8, 32768, 6)        \
+    X(223, 4, 2, 1, 16, 32768, 4)        \
+    X(224, 8, 2, 4, 4, 32768, 4)         \
+    X(225, 8, 2, 2, 8, 16384, 6)

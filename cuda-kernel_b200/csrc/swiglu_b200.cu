@@ -464,11 +464,78 @@ int launch_layer(LayerParams L, const TpParams& tp, cudaStream_t stream) {
     return check_launch();
 }
 
+// The streaming whole-layer kernel (stream_layer_kernel); `pdl`: launched programmatically
+// after the kernel before it (SWB_PREFETCH_WEIGHTS), else cooperatively. Either way the grid
+// is no larger than the CTAs that fit on the GPU at once.
+template <int CW, int CPS, int RSPLIT, int MAXR, int TARGET, int ST, bool TP>
+int launch_stream_layer(LayerParams L, const TpParams& tp, cudaStream_t stream, bool pdl) {
+    static std::atomic<uint64_t> smem_set{0};
+    constexpr int CT = CW * 32;
+    constexpr int CB = 8 * CT / RSPLIT;
+    const int H = L.hidden, I = L.inter;
+    const bool ok = H % 8 == 0 && I % 8 == 0 && (reinterpret_cast<uintptr_t>(L.wg) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(L.wu) % 16) == 0 && (reinterpret_cast<uintptr_t>(L.wd) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(L.h) % 16) == 0 && H / 8 <= kLayerMaxJ * CT;
+    if (!ok) return fail(SWB_E_UNSUPPORTED, "streaming layer needs 16-byte rows, h and weights, and a slice of x "
+                                            "that fits the geometry");
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const int G = std::min({sms * CPS, I, H});
+    if (G > kTpMaxCtas) return fail(SWB_E_UNSUPPORTED, "grid larger than the exchange supports");
+    const int rpc1 = (I + G - 1) / G, rpc2 = (H + G - 1) / G;
+    if ((rpc2 + RSPLIT - 1) / RSPLIT > MAXR) return fail(SWB_E_UNSUPPORTED, "more y rows per CTA than the geometry holds");
+    if ((I + CB - 1) / CB > kStreamMaxBlocks) return fail(SWB_E_UNSUPPORTED, "more h blocks than the workspace holds");
+    // gate rows per stage: the target bytes, and few enough that a stage's rows (G apart) touch
+    // at most two blocks of h
+    int rs1 = std::max(1, TARGET / (4 * H));
+    rs1 = std::max(1, std::min({rs1, 1 + (CB - 1) / G, rpc1}));
+    const int stage = int(align_up(std::max<size_t>(size_t(rs1) * 4 * H, size_t(rpc2) * CB * 2), 16));
+    const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
+    int stages = ST;
+    while (stages >= 2 && stream_layout(stage, stages, CW, rpc1, rpc2).total > budget) --stages;
+    if (stages < 2) return fail(SWB_E_UNSUPPORTED, "streaming layer does not fit the geometry's shared memory");
+    L.rs1 = rs1;
+    L.stages = stages;
+    L.stage_bytes = stage;
+    const size_t smem = stream_layout(stage, stages, CW, rpc1, rpc2).total;
+    auto kernel = stream_layer_kernel<CW, CPS, RSPLIT, MAXR, TP>;
+    if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, (CW + 1) * 32, smem);
+    if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    if (per_sm * sms < G) return fail(SWB_E_UNSUPPORTED, "the streaming layer's CTAs do not fit at once");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(G));
+    cfg.blockDim = dim3((CW + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    } else {
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, L, tp);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(SWB_E_CUDA, cudaGetErrorString(e));
+    }
+    return check_launch();
+}
+
 constexpr int kLayerIds[] = {
 #define SWB_LAYER_ID(ID, CW, CPS, TGT, ST) ID,
     SWB_LAYER_CONFIGS(SWB_LAYER_ID)
 #undef SWB_LAYER_ID
+#define SWB_STREAM_ID(ID, CW, CPS, RS, MR, TGT, ST) ID,
+    SWB_STREAM_LAYER_CONFIGS(SWB_STREAM_ID)
+#undef SWB_STREAM_ID
 };
+static_assert(SWB_LAYER_WORKSPACE_BYTES == 4 * kLayerWorkspaceWords, "layer workspace words");
 
 bool is_layer_config(int64_t id) {
     for (int v : kLayerIds)
@@ -476,24 +543,31 @@ bool is_layer_config(int64_t id) {
     return false;
 }
 
+// pdl: SWB_PREFETCH_WEIGHTS, honoured by the streaming kernels (the barrier kernels are
+// always launched cooperatively).
 template <bool TP>
-int dispatch_layer_one(int64_t id, const LayerParams& L, const TpParams& tp, cudaStream_t s) {
+int dispatch_layer_one(int64_t id, const LayerParams& L, const TpParams& tp, cudaStream_t s, bool pdl) {
     switch (id) {
 #define SWB_LAYER_CASE(ID, CW, CPS, TGT, ST) \
     case ID:                                 \
         return launch_layer<CW, CPS, TGT, ST, TP>(L, tp, s);
         SWB_LAYER_CONFIGS(SWB_LAYER_CASE)
 #undef SWB_LAYER_CASE
+#define SWB_STREAM_CASE(ID, CW, CPS, RS, MR, TGT, ST) \
+    case ID:                                          \
+        return launch_stream_layer<CW, CPS, RS, MR, TGT, ST, TP>(L, tp, s, pdl);
+        SWB_STREAM_LAYER_CONFIGS(SWB_STREAM_CASE)
+#undef SWB_STREAM_CASE
         default:
             return fail(SWB_E_CONFIG);
     }
 }
 
 template <bool TP>
-int dispatch_layer(int64_t id, const LayerParams& L, const TpParams& tp, cudaStream_t s) {
-    int rc = dispatch_layer_one<TP>(id, L, tp, s);
+int dispatch_layer(int64_t id, const LayerParams& L, const TpParams& tp, cudaStream_t s, bool pdl = false) {
+    int rc = dispatch_layer_one<TP>(id, L, tp, s, pdl);
     for (int i = 0; i < 2 && rc == SWB_E_UNSUPPORTED; ++i)
-        if (kLayerIds[i] != id) rc = dispatch_layer_one<TP>(kLayerIds[i], L, tp, s);
+        if (kLayerIds[i] != id) rc = dispatch_layer_one<TP>(kLayerIds[i], L, tp, s, pdl);
     return rc;
 }
 
@@ -900,7 +974,8 @@ int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const vo
         L.hidden = hidden;
         L.inter = shard;
         L.sync = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + kTpCounterBytes);
-        return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream));
+        return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream),
+                                    (flags & SWB_PREFETCH_WEIGHTS) != 0);
     }
     const TpParams t = tp_params(tp, bd, x);
     // the gate kernel advances the call epoch; the down kernel reads it after griddepcontrol.wait
@@ -971,6 +1046,13 @@ int swb_layer_config_ids(int* out, int cap) {
 int swb_ffn_fused(int layer_config, const void* wg, const void* wu, const void* wd, const void* x, const void* bg,
                   const void* bu, const void* bd, void* h, float* y, int hidden, int inter, void* workspace,
                   void* stream) {
+    return swb_ffn_fused_ex(layer_config, wg, wu, wd, x, bg, bu, bd, h, y, hidden, inter, workspace, 0u, stream);
+}
+
+int swb_ffn_fused_ex(int layer_config, const void* wg, const void* wu, const void* wd, const void* x,
+                     const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden, int inter,
+                     void* workspace, unsigned flags, void* stream) {
+    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
     if (!is_layer_config(layer_config)) return fail(SWB_E_CONFIG);
     if (hidden <= 0 || inter <= 0 || !wg || !x || !wd) return fail(SWB_E_INPUT);
     if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
@@ -993,7 +1075,8 @@ int swb_ffn_fused(int layer_config, const void* wg, const void* wu, const void* 
     L.inter = inter;
     TpParams t;
     std::memset(&t, 0, sizeof t);
-    return dispatch_layer<false>(layer_config, L, t, static_cast<cudaStream_t>(stream));
+    return dispatch_layer<false>(layer_config, L, t, static_cast<cudaStream_t>(stream),
+                                 (flags & SWB_PREFETCH_WEIGHTS) != 0);
 }
 
 }  // extern "C"

@@ -97,6 +97,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_layer_config_count": ([], _i),
         "swb_layer_config_ids": ([ctypes.POINTER(_i), _i], _i),
         "swb_ffn_fused": ([_i] + [_vp] * 9 + [_i, _i, _vp, _vp], _i),
+        "swb_ffn_fused_ex": ([_i] + [_vp] * 9 + [_i, _i, _vp, ctypes.c_uint, _vp], _i),
         "swb_swiglu_out": ([_vp] * 6 + [_i64] * 4 + [_vp], _i),
         "swb_tp_create": ([_i, _i, _i, ctypes.POINTER(_vp)], _i),
         "swb_tp_ipc_handle": ([_vp, _vp], _i),

@@ -162,14 +162,17 @@ def layer_workspace(device: torch.device | int | None = None) -> torch.Tensor:
 
 def ffn_fused(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, bg: torch.Tensor,
               bu: torch.Tensor, bd: torch.Tensor, h: torch.Tensor, y: torch.Tensor, layer_config: int,
-              workspace: torch.Tensor, stream: int | None = None) -> None:
-    """The whole layer as one persistent kernel (gate, grid barrier, down): y fp32 [H]."""
+              workspace: torch.Tensor, stream: int | None = None, prefetch_weights: bool = False) -> None:
+    """The whole layer as one persistent kernel: y fp32 [H]. Ids 200-219 run the gate, a grid
+    barrier, then the down rows; ids 220+ stream the down rows block by block as h fills.
+    ``prefetch_weights`` (ids 220+): launched programmatically after the kernel before it."""
     inter, hidden = wg.shape
     s = _stream(x.device) if stream is None else stream
+    flags = _lib.SWB_PREFETCH_WEIGHTS if prefetch_weights else 0
     with torch.cuda.device(x.device):
-        _lib.check(_lib.lib().swb_ffn_fused(int(layer_config), wg.data_ptr(), wu.data_ptr(), wd.data_ptr(),
-                                            x.data_ptr(), _ptr(bg), _ptr(bu), _ptr(bd), h.data_ptr(), y.data_ptr(),
-                                            hidden, inter, workspace.data_ptr(), s))
+        _lib.check(_lib.lib().swb_ffn_fused_ex(int(layer_config), wg.data_ptr(), wu.data_ptr(), wd.data_ptr(),
+                                               x.data_ptr(), _ptr(bg), _ptr(bu), _ptr(bd), h.data_ptr(),
+                                               y.data_ptr(), hidden, inter, workspace.data_ptr(), flags, s))
 
 
 def ffn_tp(x: torch.Tensor, wg_shard: torch.Tensor, wu_shard: torch.Tensor, wd_shard: torch.Tensor,

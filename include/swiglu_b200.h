@@ -129,16 +129,21 @@ SWB_API int swb_ffn_noalloc(int gate_config, int down_config, const void* wg, co
                             const void* x, const void* bg, const void* bu, const void* bd, float* y, int hidden,
                             int inter, void* stream);
 
-/* The whole layer in ONE persistent kernel (no counterpart in the reference): gate
- * rows, a grid barrier, then down rows, with the weight stream running straight
- * from Wg/Wu into Wd. Same arguments and outputs as swb_ffn plus `workspace`:
- * SWB_LAYER_WORKSPACE_BYTES of 16-byte aligned device memory, zeroed once when allocated, then
- * reused by every call on one stream (calls sharing a workspace must not overlap).
+/* The whole layer in ONE persistent kernel (no counterpart in the reference), with
+ * the weight stream running straight from Wg/Wu into Wd. Layer ids 200-219: gate
+ * rows, a grid barrier, then down rows. Layer ids 220+ (streaming): no barrier --
+ * the gate's rows are spread over the CTAs so h fills in order, each finished
+ * stage's h rows are counted per block of h, and each CTA streams its rows of Wd
+ * block by block as soon as a block is complete. Same arguments and outputs as
+ * swb_ffn plus `workspace`: SWB_LAYER_WORKSPACE_BYTES of 16-byte aligned device
+ * memory, zeroed once when allocated, then reused by every call on one stream
+ * (calls sharing a workspace must not overlap; each call leaves it as it found it).
  * layer_config is a layer id (swb_layer_config_ids); a geometry that cannot hold
- * a row of the shape falls back to 200, then 203. Needs hidden and inter
- * multiples of 8 and 16-byte aligned weights (else SWB_E_UNSUPPORTED: use swb_ffn).
- * The launch is cooperative: every CTA must be resident at once. After a device
- * error (swb_device_error) zero the workspace again before the next call. */
+ * the shape falls back to 200, then 203. Needs hidden and inter multiples of 8 and
+ * 16-byte aligned weights (and h, for 220+) (else SWB_E_UNSUPPORTED: use swb_ffn).
+ * The launch is cooperative, every CTA resident at once; a streaming id under
+ * SWB_PREFETCH_WEIGHTS (swb_ffn_fused_ex) is launched programmatically instead.
+ * After a device error (swb_device_error) zero the workspace again. */
 #define SWB_LAYER_WORKSPACE_BYTES 8192
 SWB_API int swb_layer_config_count(void);
 SWB_API int swb_layer_config_ids(int* out, int cap);
@@ -213,8 +218,12 @@ SWB_API int swb_swiglu_tp_out(swb_tp_t* tp, const void* x, const void* gate_shar
  * layer's down kernel and exchange. The caller promises that no kernel issued
  * before the call writes this call's Wg or Wu; x, h and the exchange are still
  * touched only after the previous kernel has completed (griddepcontrol.wait).
- * Ignored for layer ids (the fused layer kernel). Other bits: SWB_E_INPUT. */
+ * For the streaming layer ids (220+) the whole-layer kernel is launched that way;
+ * ignored for the barrier layer ids (200-219). Other bits: SWB_E_INPUT. */
 #define SWB_PREFETCH_WEIGHTS 1u
+SWB_API int swb_ffn_fused_ex(int layer_config, const void* wg, const void* wu, const void* wd, const void* x,
+                             const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden,
+                             int inter, void* workspace, unsigned flags, void* stream);
 SWB_API int swb_ffn_ex(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
                        const void* x, const void* bg, const void* bu, const void* bd, void* h, float* y, int hidden,
                        int inter, unsigned flags, void* stream);

@@ -326,6 +326,52 @@ def test_fused_layer_kernel_matches_oracle(shape):
     assert binding.device_error() == 0
 
 
+@pytest.mark.parametrize("layer", [220, 221, 224, 225])
+def test_streaming_layer_chain_matches_plain_calls(layer):
+    """Streaming whole-layer kernels chained with SWB_PREFETCH_WEIGHTS (each launched
+    programmatically, its weight stream starting while the previous layer still runs) give
+    bit-identical outputs to plain (cooperative) calls, eagerly and in one CUDA graph, and the
+    workspace's block words come back to zero after every call."""
+    H, I = 4096, 14336
+    d = [{k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in O.normal_workload(seed, H, I).items()}
+         for seed in (0, 1)]
+    ws = binding.layer_workspace()
+    h = torch.empty(I, dtype=torch.float16, device="cuda")
+    ref = []
+    for k in range(2):
+        y = torch.empty(H, dtype=torch.float32, device="cuda")
+        binding.ffn_fused(d[k]["x"], d[k]["wg"], d[k]["wu"], d[k]["wd"], d[k]["bg"], d[k]["bu"], d[k]["bd"], h, y,
+                          layer, ws)
+        torch.cuda.synchronize()
+        ref.append(y.clone())
+    ys = [torch.empty(H, dtype=torch.float32, device="cuda") for _ in range(6)]
+    stream = torch.cuda.Stream()
+
+    def chain():
+        for k in range(6):
+            w = d[k % 2]
+            binding.ffn_fused(w["x"], w["wg"], w["wu"], w["wd"], w["bg"], w["bu"], w["bd"], h, ys[k], layer, ws,
+                              stream=stream.cuda_stream, prefetch_weights=True)
+
+    with torch.cuda.stream(stream):
+        chain()
+        stream.synchronize()
+        assert all(torch.equal(ys[k], ref[k % 2]) for k in range(6))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            chain()
+        for _ in range(3):
+            for yk in ys:
+                yk.zero_()
+            g.replay()
+            stream.synchronize()
+            assert all(torch.equal(ys[k], ref[k % 2]) for k in range(6))
+        g.reset()
+    torch.cuda.synchronize()
+    assert int(ws.view(torch.int32)[1:].abs().sum()) == 0  # done counter and block words reset
+    assert binding.device_error() == 0
+
+
 @pytest.mark.parametrize("gcfg,dcfg", [(69, 87), (33, 35), (82, 82), (96, 87)])
 def test_prefetch_chain_matches_plain_calls(gcfg, dcfg):
     """Layers chained back to back with SWB_PREFETCH_WEIGHTS (each gate starts streaming its

@@ -463,6 +463,106 @@ def test_layer_kernel_plans_cover_both_phases():
                 assert (owner == 1).all()
 
 
+# ------------------------------------------- streaming whole layer (ids 220+)
+
+STREAM_GEOMS = {220: (8, 2, 2, 8, 32768, 4), 221: (8, 1, 2, 16, 32768, 6), 222: (16, 1, 4, 8, 32768, 6),
+                223: (4, 2, 1, 16, 32768, 4), 224: (8, 2, 4, 4, 32768, 4), 225: (8, 2, 2, 8, 16384, 6)}
+STREAM_MAX_BLOCKS = 8192 // 4 - 64
+
+
+def stream_plan(cfg_id, hidden, inter):
+    """Mirror of launch_stream_layer (csrc/swiglu_b200.cu): None where the kernel refuses."""
+    cw, cps, rsplit, maxr, target, smax = STREAM_GEOMS[cfg_id]
+    ct = cw * 32
+    cb = 8 * ct // rsplit
+    if hidden % 8 or inter % 8 or hidden // 8 > 8 * ct:
+        return None
+    G = min(SMS * cps, inter, hidden)
+    rpc1, rpc2 = -(-inter // G), -(-hidden // G)
+    if -(-rpc2 // rsplit) > maxr or -(-inter // cb) > STREAM_MAX_BLOCKS:
+        return None
+    rs1 = max(1, min(max(1, target // (4 * hidden)), 1 + (cb - 1) // G, rpc1))
+    up = lambda v, a: -(-v // a) * a  # noqa: E731
+    stage = up(max(rs1 * 4 * hidden, rpc2 * cb * 2), 16)
+    budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 128
+
+    def layout(stages):
+        full = up(stages * stage, 16)
+        cnt = full + 16 * stages
+        bias = up(cnt + 4 * stages, 16)
+        part1 = up(bias + rpc1 * 8, 16)
+        part2 = up(part1 + rpc1 * cw * 8, 16)
+        return {"bias": bias, "part1": part1, "part2": part2, "total": up(part2 + rpc2 * cw * 4, 16)}
+    stages = smax
+    while stages >= 2 and layout(stages)["total"] > budget:
+        stages -= 1
+    if stages < 2:
+        return None
+    return {"G": G, "cw": cw, "ct": ct, "rsplit": rsplit, "maxr": maxr, "cb": cb, "rs1": rs1, "stage": stage,
+            "stages": stages, "rpc1": rpc1, "rpc2": rpc2, "budget": budget, "layout": layout(stages)}
+
+
+@pytest.mark.parametrize("hidden,inter", [(4096, 14336), (4096, 11008), (2048, 8192), (2048, 5632), (512, 1376),
+                                          (64, 96), (4096, 7168), (4096, 3584), (4096, 1792), (4096, 2752),
+                                          (4096, 1376), (1024, 256), (520, 1032)])
+def test_stream_layer_plans_and_coverage(hidden, inter):
+    """Every copy of stream_layer_kernel stays in its stage and in its matrix, 16-byte aligned;
+    every gate row and every Wd element is streamed once; the block words, shared arrays and
+    row slots are indexed within their sizes; a stage's gate rows touch at most two h blocks."""
+    plans = {c: stream_plan(c, hidden, inter) for c in STREAM_GEOMS}
+    assert any(p is not None for p in plans.values()), (hidden, inter)
+    for c, p in plans.items():
+        if p is None:
+            continue
+        G, cb, rs1, stage, cw = p["G"], p["cb"], p["rs1"], p["stage"], p["cw"]
+        assert p["layout"]["total"] <= p["budget"] and G <= 1024
+        nblk = -(-inter // cb)
+        gate_owner = np.zeros(inter, np.int64)
+        wd_owner = np.zeros((hidden, nblk), np.int64)
+        blk_rows = np.zeros(nblk, np.int64)
+        for b in range(G):
+            nA = (inter - b + G - 1) // G if b < inter else 0
+            assert nA <= p["rpc1"]
+            for k in range(0, nA, rs1):  # one gate stage
+                ru = min(rs1, nA - k)
+                rows = [b + (k + i) * G for i in range(ru)]
+                assert all(r < inter for r in rows)
+                assert len({r // cb for r in rows}) <= 2 and rows[-1] // cb - rows[0] // cb <= 1
+                for i, r in enumerate(rows):
+                    for dst in (i * hidden * 2, (rs1 + i) * hidden * 2):
+                        assert dst % 16 == 0 and dst + hidden * 2 <= stage
+                    assert (r * hidden * 2) % 16 == 0 and (hidden * 2) % 16 == 0
+                    gate_owner[r] += 1
+                    blk_rows[r // cb] += 1
+                assert (k + ru - 1) * cw * 2 + 2 * cw <= p["rpc1"] * cw * 2  # part1 slots
+            d0, d1 = b * hidden // G, (b + 1) * hidden // G
+            nD = d1 - d0
+            assert 1 <= nD <= p["rpc2"] <= p["rsplit"] * p["maxr"]
+            for cc in range(nblk):  # one down stage
+                c0 = cc * cb
+                seg = min(cb, inter - c0)
+                assert seg % 8 == 0
+                for r in range(nD):
+                    dst = r * cb * 2
+                    assert dst % 16 == 0 and dst + seg * 2 <= stage
+                    assert ((d0 + r) * inter * 2 + c0 * 2) % 16 == 0 and (seg * 2) % 16 == 0
+                    wd_owner[d0 + r, cc] += 1
+        assert (gate_owner == 1).all() and (wd_owner == 1).all()
+        # the block words count exactly the rows each block holds
+        assert all(blk_rows[cc] == min(cb, inter - cc * cb) for cc in range(nblk))
+        # phase-2 thread map: slot t // VPB, vector t % VPB; rows slot + RSPLIT i cover [0, rpc2) once
+        vpb = p["ct"] // p["rsplit"]
+        assert vpb % 32 == 0 and vpb * 8 == cb
+        cover = np.zeros(p["rpc2"], np.int64)
+        for slot in range(p["rsplit"]):
+            for i in range(p["maxr"]):
+                r = slot + p["rsplit"] * i
+                if r < p["rpc2"]:
+                    cover[r] += 1
+                    assert r * cw + (vpb - 1) // 32 < p["rpc2"] * cw  # part2 slot
+        assert (cover == 1).all()
+
+
 # ------------------------------------------------- grouped rows (stage_rows)
 
 def reduce_scatter(values, K):

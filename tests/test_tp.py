@@ -146,7 +146,7 @@ def test_fused_tp_single_rank_eager_and_graph_replays():
             torch.cuda.synchronize()
             assert ok()
         g.reset()
-    for layer in binding.layer_config_ids()[:3]:  # the whole rank's layer as one persistent kernel
+    for layer in binding.layer_config_ids():  # the whole rank's layer as one persistent kernel
         for _ in range(2):
             y.zero_()
             T.ffn_tp_fused(ex, x, s, bd, h, y, layer, 0)
