@@ -318,10 +318,6 @@ __host__ __device__ inline StreamLayout stream_layout(int stage_bytes, int stage
     return Y;
 }
 
-__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 // Waits (bounded) until *p >= target. On time-out records SWB_DEVERR_TIMEOUT, returns false.
 __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target) {
     if (ld_acquire_gpu(p) >= target) return true;
