@@ -278,42 +278,49 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
 //
 // stream_layer_kernel (layer ids 220+): the whole layer in one persistent kernel
 // with no grid barrier. Phase 1 gives CTA b the gate rows b, b + G, b + 2G, ... so
-// that the grid writes h in ascending order; the last consumer warp to finish a
-// ring stage writes that stage's h rows and counts them, with release semantics,
-// in the word of their column block (CB = 8 * CT / RSPLIT elements of h). Phase 2
-// gives CTA b the contiguous rows [d0, d1) of y and streams them block by block:
-// a stage holds the block's CB columns of each of the CTA's rows, and the
-// consumers read it as soon as the block's word says that all its h elements are
-// written (acquire, bounded wait). A CTA therefore waits only for the blocks the
-// slowest CTAs are still producing, while it streams and multiplies the others;
-// the one producer thread never stops: Wg/Wu rows, then Wd blocks, through one
-// ring. Consumer thread t owns vector t mod (CT / RSPLIT) of a block and rows
-// t div (CT / RSPLIT) + RSPLIT * i, accumulating each row in a register across
-// blocks; at the end each row is reduced over its threads in a fixed order, so
-// the result is deterministic. The last CTA to finish resets the block words (and,
-// tensor parallel, advances the exchange epoch every CTA read at its start), so
-// calls need no clearing; after a device error zero the words again. Launched
-// cooperatively, or programmatically after the kernel before it in the stream
-// (SWB_PREFETCH_WEIGHTS): then the grid is no larger than what fits at once, and
-// a CTA that is not yet resident only makes the others wait.
+// that the grid writes h in ascending order; phase 2 gives CTA b the contiguous
+// rows [d0, d1) of y and streams them block by block: a ring stage holds the
+// block's CB columns of each of the CTA's rows (CB = 8 * CT / RSPLIT elements of h).
+// Warps: CW consumers; one producer thread streaming Wg/Wu rows, then Wd blocks,
+// through one ring without a break; and one "h warp" that keeps every global
+// round trip off the ring's path. In phase 1 the h warp takes each finished gate
+// stage's row sums (shared memory), writes the stage's h rows and counts them --
+// a fence, then a relaxed add -- in the word of their block. In phase 2 it waits
+// (bounded) until a block's word says all its h elements are written, copies the
+// block of h into a two-slot shared ring and signals the consumers on an mbarrier.
+// A CTA therefore waits only for the blocks the slowest CTAs are still producing,
+// while it streams and multiplies the others. Consumer thread t owns vector
+// t mod (CT / RSPLIT) of a block and rows t div (CT / RSPLIT) + RSPLIT * i, each
+// accumulated in a register across blocks; at the end each row is reduced over
+// its threads in a fixed order, so the result is deterministic. The last CTA to
+// finish resets the block words (and, tensor parallel, advances the exchange epoch
+// every CTA read at its start), so calls need no clearing; after a device error
+// zero the words again. Launched cooperatively, or programmatically after the
+// kernel before it in the stream (SWB_PREFETCH_WEIGHTS): then the grid is no larger
+// than what fits at once, and a CTA that is not yet resident only makes others wait.
 constexpr int kLayerWorkspaceWords = 2048;  // SWB_LAYER_WORKSPACE_BYTES / 4
 constexpr int kStreamCountBase = 64;       // first block word in LayerParams::sync
 constexpr int kStreamMaxBlocks = kLayerWorkspaceWords - kStreamCountBase;
+constexpr int kStreamHSlots = 2;           // blocks of h staged in shared memory
 
 struct StreamLayout {
-    size_t ring, full, empty, cnt, bias, part1, part2, total;
+    size_t ring, full, empty, gdone, hfull, hfree, hbuf, bias, part1, part2, total;
 };
 
-// rpc1 / rpc2: most gate rows / y rows of one CTA.
-__host__ __device__ inline StreamLayout stream_layout(int stage_bytes, int stages, int cw, int rpc1, int rpc2) {
+// rpc1 / rpc2: most gate rows / y rows of one CTA; units1: most gate stages of one CTA.
+__host__ __device__ inline StreamLayout stream_layout(int stage_bytes, int stages, int cw, int rpc1, int rpc2,
+                                                      int units1, int cb) {
     StreamLayout Y;
     Y.ring = 0;
     Y.full = align_up(size_t(stages) * stage_bytes, 16);
     Y.empty = Y.full + size_t(stages) * 8;
-    Y.cnt = Y.empty + size_t(stages) * 8;                         // consumer warps done per stage
-    Y.bias = align_up(Y.cnt + size_t(stages) * 4, 16);            // [row][bg, bu] of the CTA's gate rows
-    Y.part1 = align_up(Y.bias + size_t(rpc1) * 2 * 4, 16);        // [row][warp][gate, up]
-    Y.part2 = align_up(Y.part1 + size_t(rpc1) * cw * 2 * 4, 16);  // [row][warp]
+    Y.gdone = Y.empty + size_t(stages) * 8;                 // one per gate stage: its CW warps are done
+    Y.hfull = Y.gdone + size_t(units1) * 8;                 // h slot filled (h warp)
+    Y.hfree = Y.hfull + size_t(kStreamHSlots) * 8;          // h slot released (consumer warps)
+    Y.hbuf = align_up(Y.hfree + size_t(kStreamHSlots) * 8, 16);  // [slot][CB] fp32
+    Y.bias = align_up(Y.hbuf + size_t(kStreamHSlots) * cb * 4, 16);  // [row][bg, bu] of the gate rows
+    Y.part1 = align_up(Y.bias + size_t(rpc1) * 2 * 4, 16);          // [row][warp][gate, up]
+    Y.part2 = align_up(Y.part1 + size_t(rpc1) * cw * 2 * 4, 16);    // [row][warp]
     Y.total = align_up(Y.part2 + size_t(rpc2) * cw * 4, 16);
     return Y;
 }
@@ -332,7 +339,7 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target
 }
 
 template <int CW, int CPS, int RSPLIT, int MAXR, bool TP>
-__global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const LayerParams L, const TpParams tp) {
+__global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const LayerParams L, const TpParams tp) {
     constexpr int CT = CW * 32;
     constexpr int VPB = CT / RSPLIT;  // 16-byte vectors of a block row = threads per row slot
     constexpr int CB = VPB * 8;       // h elements (Wd columns) per block
@@ -350,11 +357,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
     const int nblk = (I + CB - 1) / CB;
     const int rpc1 = (I + G - 1) / G, rpc2 = (H + G - 1) / G;
     const int stages = L.stages;
-    const StreamLayout Y = stream_layout(L.stage_bytes, stages, CW, rpc1, rpc2);
+    const StreamLayout Y = stream_layout(L.stage_bytes, stages, CW, rpc1, rpc2, (rpc1 + rs1 - 1) / rs1, CB);
     unsigned char* ring = smem + Y.ring;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Y.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + Y.empty);
-    int* done_cnt = reinterpret_cast<int*>(smem + Y.cnt);
+    uint64_t* gdone = reinterpret_cast<uint64_t*>(smem + Y.gdone);
+    uint64_t* hfull = reinterpret_cast<uint64_t*>(smem + Y.hfull);
+    uint64_t* hfree = reinterpret_cast<uint64_t*>(smem + Y.hfree);
+    float* hbuf = reinterpret_cast<float*>(smem + Y.hbuf);
     float* sbias = reinterpret_cast<float*>(smem + Y.bias);
     float* part1 = reinterpret_cast<float*>(smem + Y.part1);
     float* part2 = reinterpret_cast<float*>(smem + Y.part2);
@@ -367,7 +377,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
             mbar_init(smem_u32(empty + s), CW);
-            done_cnt[s] = 0;
+        }
+        for (int j = 0; j < units1; ++j) mbar_init(smem_u32(gdone + j), CW);
+        for (int j = 0; j < kStreamHSlots; ++j) {
+            mbar_init(smem_u32(hfull + j), 1);
+            mbar_init(smem_u32(hfree + j), CW);
         }
         mbar_fence_init();
     }
@@ -411,6 +425,52 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
         return;
     }
 
+    if (warp == CW + 1) {
+        // ------------------------------------------------------- h warp
+        bool hok = true;
+        // phase 1: each gate stage's h rows, written and counted (fence, then relaxed add)
+        for (int j = 0; j < units1 && hok; ++j) {
+            if (!mbar_wait(smem_u32(gdone + j), 0u)) { hok = false; break; }
+            const int ru = min(rs1, nA - j * rs1);
+            for (int i = lane; i < ru; i += 32) {
+                const int kk = j * rs1 + i, row = b + kk * G;
+                float ga = sbias[2 * kk], ub = sbias[2 * kk + 1];
+                for (int w = 0; w < CW; ++w) {
+                    ga += part1[(size_t(kk) * CW + w) * 2];
+                    ub += part1[(size_t(kk) * CW + w) * 2 + 1];
+                }
+                L.h[row] = __float2half_rn(silu(ga) * ub);
+                __threadfence();
+                atomicAdd(blk + row / CB, 1u);
+            }
+        }
+        // phase 2: each complete block of h into the shared ring (fp32), in block order
+        for (int c = 0; c < nblk && hok; ++c) {
+            const int slot = c % kStreamHSlots;
+            if (c >= kStreamHSlots && !mbar_wait(smem_u32(hfree + slot), uint32_t(((c / kStreamHSlots) - 1) & 1))) {
+                hok = false;
+                break;
+            }
+            const int c0 = c * CB;
+            const int seg = min(CB, I - c0);
+            if (!__all_sync(0xffffffffu, wait_at_least(blk + c, uint32_t(seg)))) { hok = false; break; }
+            float* dst = hbuf + size_t(slot) * CB;
+            for (int q = lane; q < seg / 8; q += 32) {
+                const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(L.h + c0) + q);
+                const uint32_t w4[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = half2_bits_to_float2(w4[e]);
+                    dst[q * 8 + 2 * e] = f.x;
+                    dst[q * 8 + 2 * e + 1] = f.y;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(hfull + slot));  // release: the slot's stores first
+        }
+        return;
+    }
+
     // ----------------------------------------------------------- consumers
     const int t = threadIdx.x;
     for (int k = t; k < nA; k += CT) {  // biases do not depend on the previous kernel
@@ -420,27 +480,16 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
     }
     griddep_wait();  // x may be the previous kernel's output
     const uint32_t xe = TP ? *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u : 0u;  // this call's epoch
-    named_barrier_sync(1, CT);
+    named_barrier_sync(1, CT);  // sbias complete before the h warp reads it (gdone orders the rest)
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
 
-    // ---- phase 1: gate rows b + k G. Lane 0 of the last warp to finish a stage writes the
-    // stage's h rows; it counts them in their blocks' words one stage later (a fence, then
-    // relaxed adds), once those stores have long reached L2, so the fence does not hold it.
+    // ---- phase 1: gate rows b + k G; each warp reports a finished stage to the h warp
     {
         float xr[kLayerMaxJ][8];
         load_slice<CT>(L.x, H, t, false, xr);
         const int nv = H / 8;
-        int pend_blk = -1, pend_n = 0, pend_blk2 = -1, pend_n2 = 0;  // rows owed to block words (lane 0)
-        auto flush = [&]() {  // lane 0 wrote the h rows it counts here
-            if (lane == 0 && pend_n + pend_n2 > 0) {
-                __threadfence();
-                if (pend_n) atomicAdd(blk + pend_blk, uint32_t(pend_n));
-                if (pend_n2) atomicAdd(blk + pend_blk2, uint32_t(pend_n2));
-            }
-            pend_n = pend_n2 = 0;
-        };
         auto gate = [&](auto rg, auto jv) {
             constexpr int RG = decltype(rg)::value, J = decltype(jv)::value;
             for (int k = 0; k < units1; ++k) {
@@ -449,37 +498,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
                 const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
                 stage_rows<CW, kLayerMaxJ, 2, RG, J>(sw, ru, rs1, H, nv, xr, part1, k * rs1);
                 __syncwarp();
-                int done = 0;
                 if (lane == 0) {
-                    __threadfence_block();
-                    done = atomicAdd(done_cnt + s, 1);
                     mbar_arrive(smem_u32(empty + s));
-                }
-                done = __shfl_sync(0xffffffffu, done, 0);
-                flush();  // what this warp owes from an earlier stage
-                if (done % CW == CW - 1 && lane == 0) {  // the stage's last warp: its h rows
-                    __threadfence_block();
-                    const int first = (b + k * rs1 * G) / CB;
-                    int n1 = 0;
-                    for (int i = 0; i < ru; ++i) {
-                        const int kk = k * rs1 + i, row = b + kk * G;
-                        float ga = sbias[2 * kk], ub = sbias[2 * kk + 1];
-                        for (int j = 0; j < CW; ++j) {
-                            ga += part1[(size_t(kk) * CW + j) * 2];
-                            ub += part1[(size_t(kk) * CW + j) * 2 + 1];
-                        }
-                        L.h[row] = __float2half_rn(silu(ga) * ub);
-                        n1 += row / CB == first;
-                    }
-                    // the stage's rows lie in at most two consecutive blocks ((rs1 - 1) G < CB)
-                    pend_blk = first;
-                    pend_n = n1;
-                    pend_blk2 = first + 1;
-                    pend_n2 = ru - n1;
+                    mbar_arrive(smem_u32(gdone + k));  // release: this warp's partials of the stage
                 }
                 if (++s == stages) { s = 0; ph ^= 1u; }
             }
-            flush();
         };
         using I1 = std::integral_constant<int, 1>;
         using I2 = std::integral_constant<int, 2>;
@@ -492,30 +516,27 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
     }
 
     // ---- phase 2: rows [d0, d1) of Wd, block by block as h fills
-    const int slot = t / VPB, v = t % VPB;
+    const int rslot = t / VPB, v = t % VPB;
     float acc[MAXR];
 #pragma unroll
     for (int i = 0; i < MAXR; ++i) acc[i] = 0.f;
     for (int c = 0; ok && c < nblk; ++c) {
-        if (!mbar_wait(smem_u32(full + s), ph)) { ok = false; break; }
-        const int c0 = c * CB;
-        const int seg = min(CB, I - c0);
-        // every lane acquires the block's word itself before it reads the block's h
-        if (!__all_sync(0xffffffffu, wait_at_least(blk + c, uint32_t(seg)))) { ok = false; break; }
+        const int hs = c % kStreamHSlots;
+        if (!mbar_wait(smem_u32(full + s), ph) ||
+            !mbar_wait(smem_u32(hfull + hs), uint32_t((c / kStreamHSlots) & 1))) {
+            ok = false;
+            break;
+        }
+        const int seg = min(CB, I - c * CB);
         if (v * 8 < seg) {
-            float hf[8];
-            const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(L.h + c0) + v);
-            const uint32_t w4[4] = {hv.x, hv.y, hv.z, hv.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 f = half2_bits_to_float2(w4[q]);
-                hf[2 * q] = f.x;
-                hf[2 * q + 1] = f.y;
-            }
+            const float* hp = hbuf + size_t(hs) * CB + size_t(v) * 8;
+            const float4 ha = *reinterpret_cast<const float4*>(hp);
+            const float4 hb = *reinterpret_cast<const float4*>(hp + 4);
+            const float hf[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
             const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
 #pragma unroll
             for (int i = 0; i < MAXR; ++i) {
-                const int r = slot + RSPLIT * i;
+                const int r = rslot + RSPLIT * i;
                 if (r < nD) {
                     const uint4 wv = *reinterpret_cast<const uint4*>(sw + size_t(r) * CB + size_t(v) * 8);
                     const uint32_t u4[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -531,7 +552,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        if (lane == 0) {
+            mbar_arrive(smem_u32(empty + s));
+            mbar_arrive(smem_u32(hfree + hs));
+        }
         if (++s == stages) { s = 0; ph ^= 1u; }
     }
     if (!ok) s_failed = 1;
@@ -539,7 +563,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
 #pragma unroll
     for (int i = 0; i < MAXR; ++i) {
         const float a = warp_sum(acc[i]);
-        const int r = slot + RSPLIT * i;
+        const int r = rslot + RSPLIT * i;
         if (lane == 0 && r < nD) part2[size_t(r) * CW + (v >> 5)] = a;
     }
     named_barrier_sync(1, CT);
@@ -560,8 +584,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) stream_layer_kernel(const 
             tp_exchange_rows<CT>(tp, xe, H, d0, nD, L.y, row);
         }
     }
-    // The last CTA to get here resets the block words (every CTA has passed its waits)
-    // and, tensor parallel, advances the exchange epoch every CTA read at its start.
+    // The last CTA to get here resets the block words (every CTA's h warp has passed its
+    // waits: the consumers took every block it staged) and, tensor parallel, advances the
+    // exchange epoch every CTA read at its start.
     named_barrier_sync(1, CT);
     if (t == 0) {
         __threadfence();

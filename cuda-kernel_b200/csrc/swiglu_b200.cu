@@ -491,22 +491,23 @@ int launch_stream_layer(LayerParams L, const TpParams& tp, cudaStream_t stream, 
     rs1 = std::max(1, std::min({rs1, 1 + (CB - 1) / G, rpc1}));
     const int stage = int(align_up(std::max<size_t>(size_t(rs1) * 4 * H, size_t(rpc2) * CB * 2), 16));
     const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
+    const int units1 = (rpc1 + rs1 - 1) / rs1;
     int stages = ST;
-    while (stages >= 2 && stream_layout(stage, stages, CW, rpc1, rpc2).total > budget) --stages;
+    while (stages >= 2 && stream_layout(stage, stages, CW, rpc1, rpc2, units1, CB).total > budget) --stages;
     if (stages < 2) return fail(SWB_E_UNSUPPORTED, "streaming layer does not fit the geometry's shared memory");
     L.rs1 = rs1;
     L.stages = stages;
     L.stage_bytes = stage;
-    const size_t smem = stream_layout(stage, stages, CW, rpc1, rpc2).total;
+    const size_t smem = stream_layout(stage, stages, CW, rpc1, rpc2, units1, CB).total;
     auto kernel = stream_layer_kernel<CW, CPS, RSPLIT, MAXR, TP>;
     if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, (CW + 1) * 32, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, (CW + 2) * 32, smem);
     if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
     if (per_sm * sms < G) return fail(SWB_E_UNSUPPORTED, "the streaming layer's CTAs do not fit at once");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(G));
-    cfg.blockDim = dim3((CW + 1) * 32);
+    cfg.blockDim = dim3((CW + 2) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -486,20 +486,26 @@ def stream_plan(cfg_id, hidden, inter):
     stage = up(max(rs1 * 4 * hidden, rpc2 * cb * 2), 16)
     budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 128
 
+    units1 = -(-rpc1 // rs1)
+
     def layout(stages):
         full = up(stages * stage, 16)
-        cnt = full + 16 * stages
-        bias = up(cnt + 4 * stages, 16)
+        gdone = full + 16 * stages           # full, empty barriers; then one per gate stage
+        hfull = gdone + 8 * units1
+        hbuf = up(hfull + 2 * 2 * 8, 16)     # hfull, hfree: two h slots each
+        bias = up(hbuf + 2 * cb * 4, 16)
         part1 = up(bias + rpc1 * 8, 16)
         part2 = up(part1 + rpc1 * cw * 8, 16)
-        return {"bias": bias, "part1": part1, "part2": part2, "total": up(part2 + rpc2 * cw * 4, 16)}
+        return {"gdone": gdone, "hbuf": hbuf, "bias": bias, "part1": part1, "part2": part2,
+                "total": up(part2 + rpc2 * cw * 4, 16)}
     stages = smax
     while stages >= 2 and layout(stages)["total"] > budget:
         stages -= 1
     if stages < 2:
         return None
     return {"G": G, "cw": cw, "ct": ct, "rsplit": rsplit, "maxr": maxr, "cb": cb, "rs1": rs1, "stage": stage,
-            "stages": stages, "rpc1": rpc1, "rpc2": rpc2, "budget": budget, "layout": layout(stages)}
+            "stages": stages, "rpc1": rpc1, "rpc2": rpc2, "units1": units1, "budget": budget,
+            "layout": layout(stages)}
 
 
 @pytest.mark.parametrize("hidden,inter", [(4096, 14336), (4096, 11008), (2048, 8192), (2048, 5632), (512, 1376),
@@ -522,7 +528,7 @@ def test_stream_layer_plans_and_coverage(hidden, inter):
         blk_rows = np.zeros(nblk, np.int64)
         for b in range(G):
             nA = (inter - b + G - 1) // G if b < inter else 0
-            assert nA <= p["rpc1"]
+            assert nA <= p["rpc1"] and -(-nA // rs1) <= p["units1"]  # one gate-stage barrier each
             for k in range(0, nA, rs1):  # one gate stage
                 ru = min(rs1, nA - k)
                 rows = [b + (k + i) * G for i in range(ru)]
