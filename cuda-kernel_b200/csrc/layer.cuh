@@ -282,12 +282,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
 // rows [d0, d1) of y and streams them block by block: a ring stage holds the
 // block's CB columns of each of the CTA's rows (CB = 8 * CT / RSPLIT elements of h).
 // Warps: CW consumers; one producer thread streaming Wg/Wu rows, then Wd blocks,
-// through one ring without a break; and one "h warp" that keeps every global
-// round trip off the ring's path. In phase 1 the h warp takes each finished gate
-// stage's row sums (shared memory), writes the stage's h rows and counts them --
-// a fence, then a relaxed add -- in the word of their block. In phase 2 it waits
-// (bounded) until a block's word says all its h elements are written, copies the
-// block of h into a two-slot shared ring and signals the consumers on an mbarrier.
+// through one ring without a break; and two warps that keep every global round
+// trip off the ring's path. The signal warp takes each finished gate stage's row
+// sums (shared memory), writes the stage's h rows and counts them in the words of
+// their blocks -- a fence, then a relaxed add, one stage later, once the stores
+// have landed, so the fence costs little. The loader warp, from the kernel's start,
+// waits (bounded) for each block's word to say all its h elements are written and
+// copies the block into this CTA's shared copy of h, releasing a one-shot mbarrier
+// per block; the consumers of a block wait on that barrier only.
 // A CTA therefore waits only for the blocks the slowest CTAs are still producing,
 // while it streams and multiplies the others. Consumer thread t owns vector
 // t mod (CT / RSPLIT) of a block and rows t div (CT / RSPLIT) + RSPLIT * i, each
@@ -301,26 +303,26 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) layer_kernel(const LayerPa
 constexpr int kLayerWorkspaceWords = 2048;  // SWB_LAYER_WORKSPACE_BYTES / 4
 constexpr int kStreamCountBase = 64;       // first block word in LayerParams::sync
 constexpr int kStreamMaxBlocks = kLayerWorkspaceWords - kStreamCountBase;
-constexpr int kStreamHSlots = 2;           // blocks of h staged in shared memory
+constexpr int kStreamMaxInter = 16384;     // h held whole in shared memory (fp16)
 
 struct StreamLayout {
-    size_t ring, full, empty, gdone, hfull, hfree, hbuf, bias, part1, part2, total;
+    size_t ring, full, empty, gdone, hready, hsm, bias, part1, part2, total;
 };
 
-// rpc1 / rpc2: most gate rows / y rows of one CTA; units1: most gate stages of one CTA.
+// rpc1 / rpc2: most gate rows / y rows of one CTA; units1: most gate stages of one CTA;
+// nblk: blocks of h; inter: elements of h.
 __host__ __device__ inline StreamLayout stream_layout(int stage_bytes, int stages, int cw, int rpc1, int rpc2,
-                                                      int units1, int cb) {
+                                                      int units1, int nblk, int inter) {
     StreamLayout Y;
     Y.ring = 0;
     Y.full = align_up(size_t(stages) * stage_bytes, 16);
     Y.empty = Y.full + size_t(stages) * 8;
     Y.gdone = Y.empty + size_t(stages) * 8;                 // one per gate stage: its CW warps are done
-    Y.hfull = Y.gdone + size_t(units1) * 8;                 // h slot filled (h warp)
-    Y.hfree = Y.hfull + size_t(kStreamHSlots) * 8;          // h slot released (consumer warps)
-    Y.hbuf = align_up(Y.hfree + size_t(kStreamHSlots) * 8, 16);  // [slot][CB] fp32
-    Y.bias = align_up(Y.hbuf + size_t(kStreamHSlots) * cb * 4, 16);  // [row][bg, bu] of the gate rows
-    Y.part1 = align_up(Y.bias + size_t(rpc1) * 2 * 4, 16);          // [row][warp][gate, up]
-    Y.part2 = align_up(Y.part1 + size_t(rpc1) * cw * 2 * 4, 16);    // [row][warp]
+    Y.hready = Y.gdone + size_t(units1) * 8;                // one per block: copied into hsm (loader warp)
+    Y.hsm = align_up(Y.hready + size_t(nblk) * 8, 16);      // [inter] fp16: this CTA's copy of h
+    Y.bias = align_up(Y.hsm + size_t(inter) * 2, 16);       // [row][bg, bu] of the gate rows
+    Y.part1 = align_up(Y.bias + size_t(rpc1) * 2 * 4, 16);        // [row][warp][gate, up]
+    Y.part2 = align_up(Y.part1 + size_t(rpc1) * cw * 2 * 4, 16);  // [row][warp]
     Y.total = align_up(Y.part2 + size_t(rpc2) * cw * 4, 16);
     return Y;
 }
@@ -339,7 +341,7 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target
 }
 
 template <int CW, int CPS, int RSPLIT, int MAXR, bool TP>
-__global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const LayerParams L, const TpParams tp) {
+__global__ void __launch_bounds__((CW + 3) * 32, CPS) stream_layer_kernel(const LayerParams L, const TpParams tp) {
     constexpr int CT = CW * 32;
     constexpr int VPB = CT / RSPLIT;  // 16-byte vectors of a block row = threads per row slot
     constexpr int CB = VPB * 8;       // h elements (Wd columns) per block
@@ -357,14 +359,13 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
     const int nblk = (I + CB - 1) / CB;
     const int rpc1 = (I + G - 1) / G, rpc2 = (H + G - 1) / G;
     const int stages = L.stages;
-    const StreamLayout Y = stream_layout(L.stage_bytes, stages, CW, rpc1, rpc2, (rpc1 + rs1 - 1) / rs1, CB);
+    const StreamLayout Y = stream_layout(L.stage_bytes, stages, CW, rpc1, rpc2, (rpc1 + rs1 - 1) / rs1, nblk, I);
     unsigned char* ring = smem + Y.ring;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Y.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + Y.empty);
     uint64_t* gdone = reinterpret_cast<uint64_t*>(smem + Y.gdone);
-    uint64_t* hfull = reinterpret_cast<uint64_t*>(smem + Y.hfull);
-    uint64_t* hfree = reinterpret_cast<uint64_t*>(smem + Y.hfree);
-    float* hbuf = reinterpret_cast<float*>(smem + Y.hbuf);
+    uint64_t* hready = reinterpret_cast<uint64_t*>(smem + Y.hready);
+    __half* hsm = reinterpret_cast<__half*>(smem + Y.hsm);
     float* sbias = reinterpret_cast<float*>(smem + Y.bias);
     float* part1 = reinterpret_cast<float*>(smem + Y.part1);
     float* part2 = reinterpret_cast<float*>(smem + Y.part2);
@@ -379,10 +380,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
             mbar_init(smem_u32(empty + s), CW);
         }
         for (int j = 0; j < units1; ++j) mbar_init(smem_u32(gdone + j), CW);
-        for (int j = 0; j < kStreamHSlots; ++j) {
-            mbar_init(smem_u32(hfull + j), 1);
-            mbar_init(smem_u32(hfree + j), CW);
-        }
+        for (int c = 0; c < nblk; ++c) mbar_init(smem_u32(hready + c), 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -426,47 +424,49 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
     }
 
     if (warp == CW + 1) {
-        // ------------------------------------------------------- h warp
-        bool hok = true;
-        // phase 1: each gate stage's h rows, written and counted (fence, then relaxed add)
-        for (int j = 0; j < units1 && hok; ++j) {
-            if (!mbar_wait(smem_u32(gdone + j), 0u)) { hok = false; break; }
+        // ------------------------------------------------------- signal warp
+        // each gate stage's h rows (lane i: row i of the stage), written now and counted one
+        // stage later: fence (the stores have long landed), then a relaxed add
+        int pend = -1;
+        for (int j = 0; j < units1; ++j) {
+            if (!mbar_wait(smem_u32(gdone + j), 0u)) break;
+            if (pend >= 0) {
+                __threadfence();
+                atomicAdd(blk + pend / CB, 1u);
+                pend = -1;
+            }
             const int ru = min(rs1, nA - j * rs1);
-            for (int i = lane; i < ru; i += 32) {
-                const int kk = j * rs1 + i, row = b + kk * G;
+            if (lane < ru) {
+                const int kk = j * rs1 + lane, row = b + kk * G;
                 float ga = sbias[2 * kk], ub = sbias[2 * kk + 1];
                 for (int w = 0; w < CW; ++w) {
                     ga += part1[(size_t(kk) * CW + w) * 2];
                     ub += part1[(size_t(kk) * CW + w) * 2 + 1];
                 }
                 L.h[row] = __float2half_rn(silu(ga) * ub);
-                __threadfence();
-                atomicAdd(blk + row / CB, 1u);
+                pend = row;
             }
         }
-        // phase 2: each complete block of h into the shared ring (fp32), in block order
-        for (int c = 0; c < nblk && hok; ++c) {
-            const int slot = c % kStreamHSlots;
-            if (c >= kStreamHSlots && !mbar_wait(smem_u32(hfree + slot), uint32_t(((c / kStreamHSlots) - 1) & 1))) {
-                hok = false;
-                break;
-            }
+        if (pend >= 0) {
+            __threadfence();
+            atomicAdd(blk + pend / CB, 1u);
+        }
+        return;
+    }
+
+    if (warp == CW + 2) {
+        // ------------------------------------------------------- loader warp
+        // The block words of this call start at zero only once the kernel before has ended
+        // (the last CTA of the previous call resets them): wait for it first.
+        griddep_wait();
+        for (int c = 0; c < nblk; ++c) {
             const int c0 = c * CB;
             const int seg = min(CB, I - c0);
-            if (!__all_sync(0xffffffffu, wait_at_least(blk + c, uint32_t(seg)))) { hok = false; break; }
-            float* dst = hbuf + size_t(slot) * CB;
-            for (int q = lane; q < seg / 8; q += 32) {
-                const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(L.h + c0) + q);
-                const uint32_t w4[4] = {hv.x, hv.y, hv.z, hv.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = half2_bits_to_float2(w4[e]);
-                    dst[q * 8 + 2 * e] = f.x;
-                    dst[q * 8 + 2 * e + 1] = f.y;
-                }
-            }
+            if (!__all_sync(0xffffffffu, wait_at_least(blk + c, uint32_t(seg)))) break;
+            for (int q = lane; q < seg / 8; q += 32)
+                reinterpret_cast<uint4*>(hsm + c0)[q] = __ldcg(reinterpret_cast<const uint4*>(L.h + c0) + q);
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(hfull + slot));  // release: the slot's stores first
+            if (lane == 0) mbar_arrive(smem_u32(hready + c));  // release: the block's copies first
         }
         return;
     }
@@ -480,12 +480,12 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
     }
     griddep_wait();  // x may be the previous kernel's output
     const uint32_t xe = TP ? *reinterpret_cast<volatile const uint32_t*>(tp.ctr) + 1u : 0u;  // this call's epoch
-    named_barrier_sync(1, CT);  // sbias complete before the h warp reads it (gdone orders the rest)
+    named_barrier_sync(1, CT);  // sbias complete before the signal warp reads it (gdone orders the rest)
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
 
-    // ---- phase 1: gate rows b + k G; each warp reports a finished stage to the h warp
+    // ---- phase 1: gate rows b + k G; each warp reports a finished stage to the signal warp
     {
         float xr[kLayerMaxJ][8];
         load_slice<CT>(L.x, H, t, false, xr);
@@ -521,18 +521,21 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
 #pragma unroll
     for (int i = 0; i < MAXR; ++i) acc[i] = 0.f;
     for (int c = 0; ok && c < nblk; ++c) {
-        const int hs = c % kStreamHSlots;
-        if (!mbar_wait(smem_u32(full + s), ph) ||
-            !mbar_wait(smem_u32(hfull + hs), uint32_t((c / kStreamHSlots) & 1))) {
+        if (!mbar_wait(smem_u32(full + s), ph) || !mbar_wait(smem_u32(hready + c), 0u)) {
             ok = false;
             break;
         }
         const int seg = min(CB, I - c * CB);
         if (v * 8 < seg) {
-            const float* hp = hbuf + size_t(hs) * CB + size_t(v) * 8;
-            const float4 ha = *reinterpret_cast<const float4*>(hp);
-            const float4 hb = *reinterpret_cast<const float4*>(hp + 4);
-            const float hf[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+            const uint4 hv = *reinterpret_cast<const uint4*>(hsm + size_t(c) * CB + size_t(v) * 8);
+            const uint32_t h4[4] = {hv.x, hv.y, hv.z, hv.w};
+            float hf[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = half2_bits_to_float2(h4[q]);
+                hf[2 * q] = f.x;
+                hf[2 * q + 1] = f.y;
+            }
             const __half* sw = reinterpret_cast<const __half*>(ring + size_t(s) * L.stage_bytes);
 #pragma unroll
             for (int i = 0; i < MAXR; ++i) {
@@ -552,10 +555,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
             }
         }
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(smem_u32(empty + s));
-            mbar_arrive(smem_u32(hfree + hs));
-        }
+        if (lane == 0) mbar_arrive(smem_u32(empty + s));
         if (++s == stages) { s = 0; ph ^= 1u; }
     }
     if (!ok) s_failed = 1;
@@ -584,9 +584,9 @@ __global__ void __launch_bounds__((CW + 2) * 32, CPS) stream_layer_kernel(const 
             tp_exchange_rows<CT>(tp, xe, H, d0, nD, L.y, row);
         }
     }
-    // The last CTA to get here resets the block words (every CTA's h warp has passed its
-    // waits: the consumers took every block it staged) and, tensor parallel, advances the
-    // exchange epoch every CTA read at its start.
+    // The last CTA to get here resets the block words (every CTA's loader warp has passed
+    // its waits: the consumers took every block it copied) and, tensor parallel, advances
+    // the exchange epoch every CTA read at its start.
     named_barrier_sync(1, CT);
     if (t == 0) {
         __threadfence();

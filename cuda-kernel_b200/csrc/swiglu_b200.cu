@@ -485,29 +485,30 @@ int launch_stream_layer(LayerParams L, const TpParams& tp, cudaStream_t stream, 
     const int rpc1 = (I + G - 1) / G, rpc2 = (H + G - 1) / G;
     if ((rpc2 + RSPLIT - 1) / RSPLIT > MAXR) return fail(SWB_E_UNSUPPORTED, "more y rows per CTA than the geometry holds");
     if ((I + CB - 1) / CB > kStreamMaxBlocks) return fail(SWB_E_UNSUPPORTED, "more h blocks than the workspace holds");
+    if (I > kStreamMaxInter) return fail(SWB_E_UNSUPPORTED, "h larger than the streaming layer's shared copy");
     // gate rows per stage: the target bytes, and few enough that a stage's rows (G apart) touch
     // at most two blocks of h
     int rs1 = std::max(1, TARGET / (4 * H));
     rs1 = std::max(1, std::min({rs1, 1 + (CB - 1) / G, rpc1}));
     const int stage = int(align_up(std::max<size_t>(size_t(rs1) * 4 * H, size_t(rpc2) * CB * 2), 16));
     const size_t budget = std::min(kSmemPerCtaMax, kSmemPerSm / CPS - 1024) - 128;
-    const int units1 = (rpc1 + rs1 - 1) / rs1;
+    const int units1 = (rpc1 + rs1 - 1) / rs1, nblk = (I + CB - 1) / CB;
     int stages = ST;
-    while (stages >= 2 && stream_layout(stage, stages, CW, rpc1, rpc2, units1, CB).total > budget) --stages;
+    while (stages >= 2 && stream_layout(stage, stages, CW, rpc1, rpc2, units1, nblk, I).total > budget) --stages;
     if (stages < 2) return fail(SWB_E_UNSUPPORTED, "streaming layer does not fit the geometry's shared memory");
     L.rs1 = rs1;
     L.stages = stages;
     L.stage_bytes = stage;
-    const size_t smem = stream_layout(stage, stages, CW, rpc1, rpc2, units1, CB).total;
+    const size_t smem = stream_layout(stage, stages, CW, rpc1, rpc2, units1, nblk, I).total;
     auto kernel = stream_layer_kernel<CW, CPS, RSPLIT, MAXR, TP>;
     if (int rc = ensure_smem(kernel, smem_set, smem)) return rc;
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, (CW + 2) * 32, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, (CW + 3) * 32, smem);
     if (e != cudaSuccess) return fail(SWB_E_CUDA, cudaGetErrorString(e));
     if (per_sm * sms < G) return fail(SWB_E_UNSUPPORTED, "the streaming layer's CTAs do not fit at once");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(G));
-    cfg.blockDim = dim3((CW + 2) * 32);
+    cfg.blockDim = dim3((CW + 3) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -36,6 +36,8 @@ def main():
     p.add_argument("--reps", type=int, default=10)
     p.add_argument("--only", choices=("layer", "gate", "down"), default="layer")
     p.add_argument("--tp-ranks", type=int, default=0, help="profile one rank's fused layer at I / n rows")
+    p.add_argument("--layer-config", type=int, default=0,
+                   help="a whole-layer id (swb_ffn_fused): --only layer runs that kernel instead of the pair")
     p.add_argument("--min-bytes", type=float, default=300e6, help="total weight bytes across copies")
     a = p.parse_args()
 
@@ -87,6 +89,7 @@ def main():
     if a.tp_ranks:
         from swiglu_b200.tp import Exchange
         ex = Exchange(0, 1, H, dev)
+    ws = torch.zeros(_lib.SWB_LAYER_WORKSPACE_BYTES, dtype=torch.uint8, device=dev)
     for k, (gc, dc) in enumerate(plan):
         print(f"plan {k}: {a.reps} x {a.only} gate {gc} down {dc}", flush=True)
     with torch.cuda.stream(stream):
@@ -94,9 +97,13 @@ def main():
             for i in range(a.reps):
                 s = sets[i % copies]
                 if ex is not None:
-                    rc = L.swb_ffn_tp_fused(ex.handle, gc, dc, s["wg"].data_ptr(), s["wu"].data_ptr(),
-                                            s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(), bu.data_ptr(),
-                                            bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, I, sp)
+                    rc = L.swb_ffn_tp_fused(ex.handle, a.layer_config or gc, dc, s["wg"].data_ptr(),
+                                            s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(), bg.data_ptr(),
+                                            bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, I, sp)
+                elif a.only == "layer" and a.layer_config:
+                    rc = L.swb_ffn_fused(a.layer_config, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(),
+                                         x.data_ptr(), bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(),
+                                         y.data_ptr(), H, I, ws.data_ptr(), sp)
                 elif a.only == "layer":
                     rc = L.swb_ffn(gc, dc, s["wg"].data_ptr(), s["wu"].data_ptr(), s["wd"].data_ptr(), x.data_ptr(),
                                    bg.data_ptr(), bu.data_ptr(), bd.data_ptr(), h.data_ptr(), y.data_ptr(), H, I, sp)

@@ -466,7 +466,8 @@ def test_layer_kernel_plans_cover_both_phases():
 # ------------------------------------------- streaming whole layer (ids 220+)
 
 STREAM_GEOMS = {220: (8, 2, 2, 8, 32768, 4), 221: (8, 1, 2, 16, 32768, 6), 222: (16, 1, 4, 8, 32768, 6),
-                223: (4, 2, 1, 16, 32768, 4), 224: (8, 2, 4, 4, 32768, 4), 225: (8, 2, 2, 8, 16384, 6)}
+                223: (4, 2, 1, 16, 32768, 4), 224: (8, 2, 4, 4, 16384, 6), 225: (8, 2, 2, 8, 16384, 6),
+                226: (16, 1, 8, 4, 16384, 12)}
 STREAM_MAX_BLOCKS = 8192 // 4 - 64
 
 
@@ -487,16 +488,19 @@ def stream_plan(cfg_id, hidden, inter):
     budget = min(SMEM_PER_CTA, SMEM_PER_SM // cps - 1024) - 128
 
     units1 = -(-rpc1 // rs1)
+    nblk = -(-inter // cb)
+    if inter > 16384:  # h is held whole in shared memory
+        return None
 
     def layout(stages):
         full = up(stages * stage, 16)
         gdone = full + 16 * stages           # full, empty barriers; then one per gate stage
-        hfull = gdone + 8 * units1
-        hbuf = up(hfull + 2 * 2 * 8, 16)     # hfull, hfree: two h slots each
-        bias = up(hbuf + 2 * cb * 4, 16)
+        hready = gdone + 8 * units1          # one per block of h
+        hsm = up(hready + 8 * nblk, 16)      # the CTA's fp16 copy of h
+        bias = up(hsm + inter * 2, 16)
         part1 = up(bias + rpc1 * 8, 16)
         part2 = up(part1 + rpc1 * cw * 8, 16)
-        return {"gdone": gdone, "hbuf": hbuf, "bias": bias, "part1": part1, "part2": part2,
+        return {"gdone": gdone, "hsm": hsm, "bias": bias, "part1": part1, "part2": part2,
                 "total": up(part2 + rpc2 * cw * 4, 16)}
     stages = smax
     while stages >= 2 and layout(stages)["total"] > budget:
@@ -554,8 +558,12 @@ def test_stream_layer_plans_and_coverage(hidden, inter):
                     assert ((d0 + r) * inter * 2 + c0 * 2) % 16 == 0 and (seg * 2) % 16 == 0
                     wd_owner[d0 + r, cc] += 1
         assert (gate_owner == 1).all() and (wd_owner == 1).all()
-        # the block words count exactly the rows each block holds
+        # the block words count exactly the rows each block holds; the loader's 16-byte copies of
+        # a block stay inside the shared copy of h
         assert all(blk_rows[cc] == min(cb, inter - cc * cb) for cc in range(nblk))
+        for cc in range(nblk):
+            c0, seg = cc * cb, min(cb, inter - cc * cb)
+            assert (c0 * 2) % 16 == 0 and c0 + (seg // 8) * 8 <= inter and seg % 8 == 0
         # phase-2 thread map: slot t // VPB, vector t % VPB; rows slot + RSPLIT i cover [0, rpc2) once
         vpb = p["ct"] // p["rsplit"]
         assert vpb % 32 == 0 and vpb * 8 == cb
