@@ -111,8 +111,4 @@
 #define SWB_STREAM_LAYER_CONFIGS(X)     \
     X(220, 8, 2, 2, 8, 32768, 4)         \
     X(221, 8, 1, 2, 16, 32768, 6)        \
-    X(222, 16, 1, 4, 8, 32768, 6)        \
-    X(223, 4, 2, 1, 16, 32768, 4)        \
-    X(224, 8, 2, 4, 4, 16384, 6)         \
-    X(225, 8, 2, 2, 8, 16384, 6)         \
-    X(226, 16, 1, 8, 4, 16384, 12)
+    X(223, 4, 2, 1, 16, 32768, 4)

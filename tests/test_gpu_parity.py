@@ -326,7 +326,7 @@ def test_fused_layer_kernel_matches_oracle(shape):
     assert binding.device_error() == 0
 
 
-@pytest.mark.parametrize("layer", [220, 221, 224, 225])
+@pytest.mark.parametrize("layer", [220, 221, 223])
 def test_streaming_layer_chain_matches_plain_calls(layer):
     """Streaming whole-layer kernels chained with SWB_PREFETCH_WEIGHTS (each launched
     programmatically, its weight stream starting while the previous layer still runs) give

@@ -465,9 +465,7 @@ def test_layer_kernel_plans_cover_both_phases():
 
 # ------------------------------------------- streaming whole layer (ids 220+)
 
-STREAM_GEOMS = {220: (8, 2, 2, 8, 32768, 4), 221: (8, 1, 2, 16, 32768, 6), 222: (16, 1, 4, 8, 32768, 6),
-                223: (4, 2, 1, 16, 32768, 4), 224: (8, 2, 4, 4, 16384, 6), 225: (8, 2, 2, 8, 16384, 6),
-                226: (16, 1, 8, 4, 16384, 12)}
+STREAM_GEOMS = {220: (8, 2, 2, 8, 32768, 4), 221: (8, 1, 2, 16, 32768, 6), 223: (4, 2, 1, 16, 32768, 4)}
 STREAM_MAX_BLOCKS = 8192 // 4 - 64
 
 

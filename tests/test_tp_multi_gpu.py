@@ -68,14 +68,14 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
     from swiglu_b200 import tp as T
     ex = T.Exchange(rank, world, hidden, dev)
     s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
-    for gate, down in ((69, 80), (69, 83), (69, 87), (69, 87), (200, 0), (201, 0), (200, 0), (220, 0), (224, 0),
-                       (222, 0)):
+    for gate, down in ((69, 80), (69, 83), (69, 87), (69, 87), (200, 0), (201, 0), (200, 0), (220, 0), (223, 0),
+                       (221, 0)):
         y.zero_()
         T.ffn_tp_fused(ex, x, s, bd, h, y, gate, down)  # 200+: the rank's whole layer in one kernel
         torch.cuda.synchronize()
         out.append(y.cpu().numpy().copy())
     # geometries switched back to back with no host synchronisation: every call keeps its own y
-    seq = [(69, 80), (200, 0), (69, 87), (220, 0), (201, 0), (69, 83), (224, 0), (69, 80)] * 3
+    seq = [(69, 80), (200, 0), (69, 87), (220, 0), (201, 0), (69, 83), (223, 0), (69, 80)] * 3
     ys = [torch.empty_like(y) for _ in seq]
     for (gate, down), yk in zip(seq, ys):
         T.ffn_tp_fused(ex, x, s, bd, h, yk, gate, down)
