@@ -490,9 +490,7 @@ __host__ __device__ inline BulkLayout rbulk_layout(int nm, int row_stage, int co
     const size_t off = size_t(stages) * row_stage * nm * size_t(cols) * 2;
     L.full = align_up(off, 16);
     L.empty = L.full + size_t(stages) * 8;
-    // per-stage count of consumer warps done (rbulk_stream's stage hook), then the row
-    // partials; no x copy: x lives in registers
-    L.xs = align_up(L.empty + size_t(stages) * 8 + size_t(stages) * 4, 16);
+    L.xs = align_up(L.empty + size_t(stages) * 8, 16);  // no x copy: x lives in registers
     L.part = L.xs;
     L.total = align_up(L.part + size_t(rows_per_cta) * cw * nm * 4, 16);
     return L;
@@ -577,20 +575,9 @@ __device__ __forceinline__ void stage_rows(const __half* sw, int ru, int rs, int
     }
 }
 
-// Called by the last consumer warp to finish a ring stage, once per stage, after that
-// warp has released the stage, with the CTA's partials, its first row, the stage's
-// first local row, its row count, the lane and the call epoch (read once per warp);
-// every warp's partials of those rows are in shared memory by then. The plain kernels
-// pass NoStageHook (no counting).
-struct NoStageHook {
-    static constexpr bool kActive = false;
-    __device__ void operator()(const float*, int, int, int, int, uint32_t) const {}
-};
-
-template <int CW, int MAXJ, int MODE, class Hook = NoStageHook>
+template <int CW, int MAXJ, int MODE>
 __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* smem, int& r0_out, int& nrows_out,
-                                             float*& part_out, uint32_t* epoch_out = nullptr,
-                                             const Hook& hook = Hook()) {
+                                             float*& part_out, uint32_t* epoch_out = nullptr) {
     constexpr bool GATED = MODE == MODE_GATE;
     constexpr int NM = GATED ? 2 : 1;
     constexpr int CT = CW * 32;
@@ -613,7 +600,6 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
     __half* ring = reinterpret_cast<__half*>(smem + L.ring);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
-    int* done_cnt = reinterpret_cast<int*>(smem + L.empty + size_t(stages) * 8);
     float* part = reinterpret_cast<float*>(smem + L.part);
     r0_out = r0;
     nrows_out = nrows;
@@ -625,7 +611,6 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
             mbar_init(smem_u32(empty + s), CW);
-            done_cnt[s] = 0;
         }
         mbar_fence_init();
     }
@@ -665,10 +650,8 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
     griddep_wait();  // x may be the previous kernel's output (h of the gate stage)
     // the fused tensor-parallel down kernel reads the call epoch its gate advanced;
     // as the gate of a tensor-parallel call this kernel advances it
-    uint32_t epoch = 0;  // the call epoch, for the stage hook (read once, after the gate completed)
     if (epoch_out) {
-        epoch = *reinterpret_cast<volatile const uint32_t*>(p.epoch);
-        if (t == 0) *epoch_out = epoch;
+        if (t == 0) *epoch_out = *reinterpret_cast<volatile const uint32_t*>(p.epoch);
     } else {
         advance_call_epoch(p, blockIdx.x == 0);
     }
@@ -713,26 +696,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
             const __half* sw = ring + size_t(s) * stage_halves;
             stage_rows<CW, MAXJ, NM, RG, J>(sw, ru, rs, cols, nv, xr, part, row0 - r0);
             __syncwarp();
-            if constexpr (Hook::kActive) {
-                // Count this warp done with the stage, release the stage, and if it was the
-                // last of the CW warps run the hook on the stage's rows (the hook reads only
-                // the partials, never the ring). The count only grows: every warp counts a
-                // pass before it releases the stage, and the next pass of the stage needs all
-                // CW releases, so the last warp of each pass sees a count of CW - 1 mod CW.
-                int done = 0;
-                if (lane == 0) {
-                    __threadfence_block();
-                    done = atomicAdd(done_cnt + s, 1);
-                    mbar_arrive(smem_u32(empty + s));
-                }
-                done = __shfl_sync(0xffffffffu, done, 0);
-                if (done % CW == CW - 1) {
-                    __threadfence_block();
-                    hook(part, r0, row0 - r0, ru, lane, epoch);
-                }
-            } else {
-                if (lane == 0) mbar_arrive(smem_u32(empty + s));
-            }
+            if (lane == 0) mbar_arrive(smem_u32(empty + s));
             if (++s == stages) { s = 0; ph ^= 1u; }
         }
     };
@@ -801,25 +765,20 @@ struct TpParams {
 __device__ __forceinline__ void store_out(float* y, int i, float v) { y[i] = v; }
 __device__ __forceinline__ void store_out(__half* y, int i, float v) { y[i] = __float2half_rn(v); }
 
-// Stores this rank's partial `v` of row `row` into slot [parity][my rank][row] of every
-// other rank's buffer (one 64-bit word each, with the epoch).
-__device__ __forceinline__ void tp_send_row(const TpParams& tp, uint32_t epoch, int rows, int row, float v) {
+template <int CT, class Out, class Own>
+__device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, Out* y,
+                                                 Own own) {
     // rank loops run to the compile-time bound, so recv[] is indexed by constants
     // and stays in the kernel's parameter space
-    const size_t par = epoch & 1u;
-#pragma unroll
-    for (int q = 0; q < kTpMaxRanks; ++q)
-        if (q < tp.world && q != tp.rank) st_slot_sys(tp.recv[q] + (par * tp.world + tp.rank) * rows + row, v, epoch);
-}
-
-// Rows [r0, r0 + n) of y, once every rank's partial has been sent: each row waits for the
-// peers' words of this epoch and sums every rank's partial in rank order -- the same order
-// on every rank, so y is bit-identical everywhere -- plus bias and residual.
-template <int CT, class Out, class Own>
-__device__ __forceinline__ void tp_collect_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, Out* y,
-                                                Own own) {
     const int t = threadIdx.x;
     const size_t par = epoch & 1u;
+    for (int i = t; i < n; i += CT) {
+        const float a = own(i);
+#pragma unroll
+        for (int q = 0; q < kTpMaxRanks; ++q)
+            if (q < tp.world && q != tp.rank)
+                st_slot_sys(tp.recv[q] + (par * tp.world + tp.rank) * rows + r0 + i, a, epoch);
+    }
     const unsigned long long* mine = tp.recv[0] + par * tp.world * rows;
 #pragma unroll
     for (int q = 1; q < kTpMaxRanks; ++q)
@@ -843,31 +802,6 @@ __device__ __forceinline__ void tp_collect_rows(const TpParams& tp, uint32_t epo
     }
 }
 
-// Rows [r0, r0 + n) of y: this rank's partial `own(i)` goes to every other rank, then the
-// rows are collected (tp_collect_rows). A rank can run at most one call ahead of a peer
-// (each call waits for that peer's slots), so the parity double buffer keeps a slot from
-// being rewritten before it is read.
-template <int CT, class Out, class Own>
-__device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t epoch, int rows, int r0, int n, Out* y,
-                                                 Own own) {
-    for (int i = threadIdx.x; i < n; i += CT) tp_send_row(tp, epoch, rows, r0 + i, own(i));
-    tp_collect_rows<CT>(tp, epoch, rows, r0, n, y, own);
-}
-
-// Stage hook of the fused down kernel: the rows of a finished stage go to the peers at
-// once, so their NVLink stores overlap the stages still streaming, and only the last
-// stage's stores are in flight when the CTA starts collecting.
-template <int CW>
-struct TpStageSend {
-    static constexpr bool kActive = true;
-    const TpParams& tp;
-    const Params& p;
-    __device__ void operator()(const float* part, int r0, int lrow0, int ru, int lane, uint32_t epoch) const {
-        for (int r = lane; r < ru; r += 32)
-            tp_send_row(tp, epoch, p.rows, r0 + lrow0 + r, row_sum<CW, 1>(part, lrow0 + r, 0));
-    }
-};
-
 // The down projection of a tensor-parallel rank with the all-reduce fused into
 // its epilogue (tp_exchange_rows). Every rank runs the same grid and row
 // partition, so CTA b owns rows [r0, r1) of y on every rank. The epoch lives in
@@ -881,14 +815,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_allreduce_kernel(con
     __shared__ uint32_t s_epoch;
     int r0, nrows;
     float* part;
-    const TpStageSend<CW> send{tp, p};
-    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part, &s_epoch, send)) return;
+    if (!rbulk_stream<CW, MAXJ, MODE_F32>(p, smem, r0, nrows, part, &s_epoch)) return;
     named_barrier_sync(1, CT);
     auto own = [&](int i) { return row_sum<CW, 1>(part, i, 0); };
     if constexpr (HALF_OUT)
-        tp_collect_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.h, own);
+        tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.h, own);
     else
-        tp_collect_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.y, own);
+        tp_exchange_rows<CT>(tp, s_epoch, p.rows, r0, nrows, p.y, own);
 }
 
 // ===================================================================== SBULK

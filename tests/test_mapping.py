@@ -174,10 +174,8 @@ def rbulk_layout(nm, rs, cols, stages, cw, rows_per_cta):
         return (v + a - 1) // a * a
     full = up(stages * rs * nm * cols * 2, 16)
     empty = full + stages * 8
-    cnt = empty + stages * 8  # consumer warps done per stage (the fused exchange's send hook)
-    part = up(cnt + stages * 4, 16)
-    return {"full": full, "empty": empty, "cnt": cnt, "part": part,
-            "total": up(part + rows_per_cta * cw * nm * 4, 16)}
+    part = up(empty + stages * 8, 16)
+    return {"full": full, "empty": empty, "part": part, "total": up(part + rows_per_cta * cw * nm * 4, 16)}
 
 
 def rbulk_plan(cfg, rows, cols, gated, w_aligned=True):
