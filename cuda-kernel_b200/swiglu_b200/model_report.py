@@ -114,7 +114,7 @@ def render(data: dict) -> str:
     found = problems(data)
     if found:
         raise ValueError(f"{len(found)} problem(s) in the model evidence: " + "; ".join(found))
-    extra = [f"{k} {data[k]}" for k in ("ranks", "decode") if data.get(k)]
+    extra = [f"{data['ranks']} tensor-parallel ranks"] if (data.get("ranks") or 1) > 1 else []
     lines = [f"`{data['model']}` (revision `{data['resolved_revision']}`) on {data['gpu']}: fp16, batch 1, "
              f"{data['patched_layers']} decode MLPs replaced" + (f", {', '.join(extra)}" if extra else "") + ".",
              "Both sides prefill with the stock model and decode the same way ("
