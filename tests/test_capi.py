@@ -196,6 +196,26 @@ def test_layer_registry_and_fused_guards():
     assert b"16-byte aligned" in L().swb_last_error()
     assert f(200, None, *([FAKE] * 8), 64, 96, FAKE, None) == _lib.SWB_E_INPUT
     assert f(200, FAKE, None, *([FAKE] * 7), 64, 96, FAKE, None) == _lib.SWB_E_GATE_BUFFERS
+    # the streaming ids are layer ids too; the flags variant rejects unknown bits first
+    assert {220, 221, 223} <= set(ids)
+    fx = L().swb_ffn_fused_ex
+    assert fx(220, *([FAKE] * 9), 64, 96, FAKE, 2, None) == _lib.SWB_E_INPUT
+    assert b"flags" in L().swb_last_error()
+    assert fx(33, *([FAKE] * 9), 64, 96, FAKE, _lib.SWB_PREFETCH_WEIGHTS, None) == _lib.SWB_E_CONFIG
+    assert fx(220, *([FAKE] * 9), 64, 96, None, _lib.SWB_PREFETCH_WEIGHTS, None) == _lib.SWB_E_WORKSPACE
+
+
+def test_tp_model_path_and_epoch_guards_without_gpu():
+    """swb_swiglu_tp_out and swb_tp_epoch refuse a missing exchange, and unknown flags, before
+    any CUDA call."""
+    f = L().swb_swiglu_tp_out
+    assert f(None, *([FAKE] * 6), 4096, 512, 69, 87, 0, None) == _lib.SWB_E_INPUT
+    assert b"exchange" in L().swb_last_error()
+    assert f(FAKE, *([FAKE] * 6), 4096, 512, 69, 87, 4, None) == _lib.SWB_E_INPUT  # unknown flag bit
+    assert b"flags" in L().swb_last_error()
+    out = ctypes.c_uint32()
+    assert L().swb_tp_epoch(None, ctypes.byref(out)) == _lib.SWB_E_INPUT
+    assert L().swb_tp_epoch(FAKE, None) == _lib.SWB_E_INPUT
 
 
 C_CALLER = r"""
