@@ -785,14 +785,21 @@ __device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t ep
         if (q == tp.rank) mine = tp.recv[q] + par * tp.world * rows;
     bool ok = true;
     for (int i = t; i < n; i += CT) {
+        // every peer's word of this row first, the loads all in flight together; only the
+        // words that do not carry this epoch yet are then polled (bounded), one peer at a time
+        unsigned long long w[kTpMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kTpMaxRanks; ++q)
+            w[q] = (q < tp.world && q != tp.rank) ? ld_slot_sys(mine + size_t(q) * rows + r0 + i) : 0ull;
         float acc = 0.f;
 #pragma unroll
         for (int q = 0; q < kTpMaxRanks; ++q) {
             if (q >= tp.world) break;
             float v = 0.f;
             if (q == tp.rank) v = own(i);
+            else if (uint32_t(w[q] >> 32) == epoch) v = __uint_as_float(uint32_t(w[q]));
             else if (ok) ok = wait_slot(mine + size_t(q) * rows + r0 + i, epoch, v);
-            acc += v;
+            acc += v;  // rank order, whichever word came first: y is the same on every rank
         }
         if (!ok) break;  // a peer did not deliver: the error word is set, y is not written
         float add = 0.f;
