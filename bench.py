@@ -539,6 +539,22 @@ def ours(args) -> None:
                                          alone_us(lambda i: layer_step(lcfg, gcfg, dcfg, i)))
     kernels["gate"] = kernel_record("gate", gcfg, gate_bytes, alone_us(lambda i: launch_gate(gcfg, i)))
     kernels["down"] = kernel_record("down", dcfg, down_bytes, alone_us(lambda i: launch_down(dcfg, i)))
+    # The pair is chosen by whole chained steps, where a deep ring prefetches more of the
+    # next kernel's weights behind this one's tail; launched alone, a shallow ring (SMs kept
+    # even) can be faster. The fastest of the three best-tuned geometries of each kernel,
+    # timed alone the same way, is recorded beside the pair's.
+    if tuned is not None:
+        for tag, launch, nbytes, pair_cfg in (("gate", launch_gate, gate_bytes, gcfg),
+                                              ("down", launch_down, down_bytes, dcfg)):
+            times = tuned[tag + "_times"]
+            cands = agree(sorted(times, key=times.get)[:3])
+            alone = {c: (kernels[tag]["launch_us"] if c == pair_cfg else
+                         alone_us(lambda i, c=c, f=launch: f(c, i)))
+                     for c in cands}
+            best = min(alone, key=alone.get)
+            rec = kernel_record(tag, best, nbytes, alone[best])
+            rec["candidates_us"] = {str(c): round(v, 3) for c, v in alone.items()}
+            kernels[tag + "_best_alone"] = rec
     dom = kernels["layer" if lcfg else "gate"]
     kname = (f"fused layer (config {lcfg})" + (" with the NVLink exchange" if world > 1 else "")) if lcfg \
         else f"gate (config {gcfg})"

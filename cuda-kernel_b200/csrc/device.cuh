@@ -23,6 +23,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
+// Timeline points of the streaming kernels, called by one thread of a CTA:
+// 0 entry, 1 first ring stage landed, 2 last stage consumed, 3 results written,
+// 4 the producer's last copy issued. A profiling build defines SWB_TIMELINE to
+// record when each CTA passes each point; the library leaves it empty.
+#ifndef SWB_TIMELINE
+#define SWB_TIMELINE(point) ((void)0)
+#endif
+
 // ---------------------------------------------------------------- loads
 
 // 128-bit read-only streaming load: weights are read exactly once, so skip L1.

@@ -375,6 +375,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
+        SWB_TIMELINE(0);
         s_failed = 0;
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
@@ -407,6 +408,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
             if (++ch == nch) { ch = 0; ++row; }
             if (++s == stages) { s = 0; ph ^= 1u; }
         }
+        SWB_TIMELINE(4);
         // Never leave with copies in flight: wait (bounded) for the last fills.
         const int drain = issued < stages ? issued : stages;
         for (int j = 1; j <= drain; ++j) {
@@ -435,6 +437,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
             s_failed = 1;
             break;
         }
+        if (k == 0 && t == 0) SWB_TIMELINE(1);
         const int c0 = ch * CHUNK;
         const int nv = min(CHUNK, cols - c0) / 8;
         const __half* sw = ring + size_t(s) * NM * CHUNK;
@@ -468,6 +471,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
         }
         if (++s == stages) { s = 0; ph ^= 1u; }
     }
+    if (t == 0) SWB_TIMELINE(2);
     named_barrier_sync(1, CT);
     if (s_failed) return;
     for (int i = t; i < nrows; i += CT) {
@@ -478,6 +482,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
         }
         write_row<MODE>(p, r0 + i, a, b);
     }
+    if (t == 0) SWB_TIMELINE(3);
 }
 
 // ===================================================================== RBULK
@@ -607,6 +612,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
+        SWB_TIMELINE(0);
         s_failed = 0;
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
@@ -637,6 +643,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
             ++issued;
             if (++s == stages) { s = 0; ph ^= 1u; }
         }
+        SWB_TIMELINE(4);
         const int drain = issued < stages ? issued : stages;
         for (int j = 1; j <= drain; ++j) {
             const int k = issued - j;
@@ -691,6 +698,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
                 s_failed = 1;
                 break;
             }
+            if (k == 0 && t == 0) SWB_TIMELINE(1);
             const int row0 = r0 + k * rs;
             const int ru = min(rs, r1 - row0);
             const __half* sw = ring + size_t(s) * stage_halves;
@@ -699,6 +707,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
             if (lane == 0) mbar_arrive(smem_u32(empty + s));
             if (++s == stages) { s = 0; ph ^= 1u; }
         }
+        if (t == 0) SWB_TIMELINE(2);
     };
     const int jn = (nv + CT - 1) / CT;
     if (jn <= 1)
@@ -729,6 +738,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) rbulk_kernel(const Params 
     if (!rbulk_stream<CW, MAXJ, MODE>(p, smem, r0, nrows, part)) return;
     for (int i = threadIdx.x; i < nrows; i += CT)
         write_row<MODE>(p, r0 + i, row_sum<CW, NM>(part, i, 0), NM == 2 ? row_sum<CW, NM>(part, i, NM - 1) : 0.f);
+    if (threadIdx.x == 0) SWB_TIMELINE(3);
 }
 
 // ============================================ RBULK + one-shot all-reduce
@@ -888,6 +898,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
+        SWB_TIMELINE(0);
         s_failed = 0;
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
@@ -966,6 +977,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
                 break;
             }
         }
+        SWB_TIMELINE(4);
         // Collect any request still outstanding (its answer is written asynchronously).
         while (q_len > 0) {
             const int slot = q_head;
@@ -1022,6 +1034,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
 
     int s = 0;
     uint32_t ph = 0;
+    bool first = true;
     while (true) {
         if (!mbar_wait(smem_u32(full + s), ph)) {
             s_failed = 1;
@@ -1029,6 +1042,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
         }
         const int2 m = meta[s];
         if (m.x < 0) break;
+        if (first && t == 0) SWB_TIMELINE(1);
+        first = false;
         // row 0 is in exactly one stage of one CTA, whichever CTA took its block
         advance_call_epoch(p, m.x == 0);
         const __half* sw = ring + size_t(s) * stage_halves;
@@ -1081,6 +1096,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CPS) sbulk_kernel(const Params 
         if (lane == 0) mbar_arrive(smem_u32(empty + s));
         if (++s == stages) { s = 0; ph ^= 1u; }
     }
+    if (t == 0) SWB_TIMELINE(2);
     (void)s_failed;
 }
 

@@ -30,6 +30,12 @@
 //   faster do more of the matrix. Falls back to id 64 like RBULK.
 #pragma once
 
+// A measurement build may append geometries to the list (ids 150-199) by
+// defining SWB_EXTRA_CONFIGS(X) before this header; the library appends none.
+#ifndef SWB_EXTRA_CONFIGS
+#define SWB_EXTRA_CONFIGS(X)
+#endif
+
 #define SWB_FAM_LDG 0
 #define SWB_FAM_BULK 1
 #define SWB_FAM_RBULK 2
@@ -79,7 +85,18 @@
     X(96, SWB_FAM_SBULK, 4, 3, 8, 4, 16384, 5)                                                  \
     X(97, SWB_FAM_SBULK, 6, 2, 8, 4, 16384, 8)                                                  \
     X(98, SWB_FAM_SBULK, 2, 4, 8, 8, 16384, 3)                                                  \
-    X(99, SWB_FAM_SBULK, 8, 3, 8, 4, 16384, 4)
+    X(99, SWB_FAM_SBULK, 8, 3, 8, 4, 16384, 4)                                                  \
+    /* Shallow rings. With every SM streaming at once the memory fabric, not the SM,  */        \
+    /* sets each SM's share, and some SMs get up to 1.4x less than others: a deep ring */        \
+    /* (over ~128 KB in flight per SM) then leaves those SMs microseconds behind at   */        \
+    /* the end of a launch. About 115-128 KB in flight per SM keeps HBM busy and the  */        \
+    /* SMs even. 100/101: long rows; 102: short rows; 103: a small gate that leaves   */        \
+    /* room for the down kernel's CTAs beside it.                                     */        \
+    X(100, SWB_FAM_RBULK, 8, 2, 8, 8, 16384, 2)                                                 \
+    X(101, SWB_FAM_RBULK, 16, 1, 8, 4, 32768, 4)                                                \
+    X(102, SWB_FAM_RBULK, 4, 2, 8, 8, 16384, 2)                                                 \
+    X(103, SWB_FAM_BULK, 8, 2, 8, 1, 2048, 4)                                                   \
+    SWB_EXTRA_CONFIGS(X)
 
 // Ids used when a BULK / RBULK geometry cannot run a shape.
 #define SWB_BULK_FALLBACK_ID 33

@@ -68,39 +68,41 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
     from swiglu_b200 import tp as T
     ex = T.Exchange(rank, world, hidden, dev)
     s = {"wg": wg, "wu": wu, "wd": wd, "bg": bg, "bu": bu}
-    for gate, down in ((69, 80), (69, 83), (69, 87), (69, 87), (200, 0), (201, 0), (200, 0), (220, 0), (223, 0),
-                       (221, 0)):
+    for gate, down in ((69, 80), (69, 83), (69, 87), (69, 87), (69, 102), (103, 102), (69, 100), (200, 0), (201, 0),
+                       (200, 0), (220, 0), (223, 0), (221, 0)):
         y.zero_()
         T.ffn_tp_fused(ex, x, s, bd, h, y, gate, down)  # 200+: the rank's whole layer in one kernel
         torch.cuda.synchronize()
         out.append(y.cpu().numpy().copy())
     # geometries switched back to back with no host synchronisation: every call keeps its own y
-    seq = [(69, 80), (200, 0), (69, 87), (220, 0), (201, 0), (69, 83), (223, 0), (69, 80)] * 3
+    seq = [(69, 80), (200, 0), (69, 87), (220, 0), (201, 0), (69, 83), (223, 0), (103, 102), (69, 80)] * 3
     ys = [torch.empty_like(y) for _ in seq]
     for (gate, down), yk in zip(seq, ys):
         T.ffn_tp_fused(ex, x, s, bd, h, yk, gate, down)
     torch.cuda.synchronize()
     out.extend(yk.cpu().numpy().copy() for yk in ys)
     # layers chained with SWB_PREFETCH_WEIGHTS in one CUDA graph: bit-identical to plain calls
-    plain = torch.empty_like(y)
-    T.ffn_tp_fused(ex, x, s, bd, h, plain, 69, 87)
-    torch.cuda.synchronize()  # calls on one exchange must not overlap (the chain runs on another stream)
-    chain_ys = [torch.empty_like(y) for _ in range(4)]
+    # (69/102: the next layer's gate CTAs fit beside the down CTAs that wait on the exchange)
     stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        for yk in chain_ys:  # warm (and NCCL-free): eager chain first
-            T.ffn_tp_fused(ex, x, s, bd, h, yk, 69, 87, stream=stream.cuda_stream, prefetch_weights=True)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+    for gate, down in ((69, 87), (69, 102)):
+        plain = torch.empty_like(y)
+        T.ffn_tp_fused(ex, x, s, bd, h, plain, gate, down)
+        torch.cuda.synchronize()  # calls on one exchange must not overlap (the chain runs on another stream)
+        chain_ys = [torch.empty_like(y) for _ in range(4)]
+        with torch.cuda.stream(stream):
+            for yk in chain_ys:  # warm (and NCCL-free): eager chain first
+                T.ffn_tp_fused(ex, x, s, bd, h, yk, gate, down, stream=stream.cuda_stream, prefetch_weights=True)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for yk in chain_ys:
+                    T.ffn_tp_fused(ex, x, s, bd, h, yk, gate, down, stream=stream.cuda_stream, prefetch_weights=True)
             for yk in chain_ys:
-                T.ffn_tp_fused(ex, x, s, bd, h, yk, 69, 87, stream=stream.cuda_stream, prefetch_weights=True)
-        for yk in chain_ys:
-            yk.zero_()
-        g.replay()
-        stream.synchronize()
-        g.reset()
-    torch.cuda.synchronize()
-    assert all(torch.equal(yk, plain) for yk in chain_ys)
+                yk.zero_()
+            g.replay()
+            stream.synchronize()
+            g.reset()
+        torch.cuda.synchronize()
+        assert all(torch.equal(yk, plain) for yk in chain_ys)
     # the model path (swiglu_out of a rank: model-rounding gate, fp16 y summed over the ranks)
     s_model = {"wg": wg, "wu": wu, "wd": wd}
     xm = x.view(1, 1, hidden)
