@@ -52,6 +52,7 @@ struct Params {
     int rows_per_block;  // sbulk_kernel: rows per CTA index (unit of work stealing)
     int blocks;          // sbulk_kernel: number of row blocks (= grid size)
     int block_stride;    // sbulk_kernel: A in row_block = (cta * A) mod blocks, gcd(A, blocks) = 1
+    int inflight;        // bulk_kernel / rbulk_kernel: copies in flight once the ring is full (0 = ring depth)
     // Tensor-parallel exchange call epoch (null otherwise): the gate kernel of a
     // call advances it (advance_call_epoch); the fused down kernel reads it after
     // griddepcontrol.wait, so both kernels of the call agree on it.
@@ -73,6 +74,22 @@ struct Params {
 // slot still holds that value.
 __device__ __forceinline__ void advance_call_epoch(const Params& p, bool owner) {
     if (p.epoch && owner && threadIdx.x == 0) atomicAdd(p.epoch, 1u);
+}
+
+// The producer's wait before issuing copy k into a ring of `stages` slots. The
+// first `stages` copies go out at once (with programmatic launch they land while
+// the previous kernel still runs); after that copy k waits until copy
+// k - depth has been consumed, so at most `depth` copies stay in flight. depth =
+// stages is the plain ring (wait for the slot's previous copy). Copies are
+// consumed in order, so copy k - depth consumed implies slot k % stages free, and
+// slot (k - depth) % stages has not started its next round: its parity is exact.
+__device__ __forceinline__ bool ring_slot_ready(const uint64_t* empty, int k, int stages, int depth) {
+    if (k < stages) return true;
+    const int j = k - depth;
+    return mbar_wait(smem_u32(empty + (j % stages)), uint32_t((j / stages) & 1));
+}
+__device__ __forceinline__ int ring_depth(const Params& p) {
+    return p.inflight > 0 && p.inflight < p.stages ? p.inflight : p.stages;
 }
 
 template <int MODE>
@@ -392,10 +409,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
         // ------------------------------------------------------- producer
         if (lane != 0) return;
         const uint64_t pol = l2_evict_first_policy();
+        const int depth = ring_depth(p);
         int s = 0, row = r0, ch = 0, issued = 0;
-        uint32_t ph = 0;
         for (int k = 0; k < units; ++k) {
-            if (k >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) break;
+            if (!ring_slot_ready(empty, k, stages, depth)) break;
             const int c0 = ch * CHUNK;
             const int len = min(CHUNK, cols - c0);
             const uint32_t bytes = uint32_t(len) * 2u;
@@ -406,7 +423,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) bulk_kernel(const Params p) 
             if constexpr (GATED) bulk_copy_g2s(smem_u32(ring + (size_t(s) * NM + 1) * CHUNK), p.u + goff, bytes, fb, pol);
             ++issued;
             if (++ch == nch) { ch = 0; ++row; }
-            if (++s == stages) { s = 0; ph ^= 1u; }
+            if (++s == stages) s = 0;
         }
         SWB_TIMELINE(4);
         // Never leave with copies in flight: wait (bounded) for the last fills.
@@ -627,10 +644,10 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
         // ------------------------------------------------------- producer
         if (lane != 0) return false;
         const uint64_t pol = l2_evict_first_policy();
+        const int depth = ring_depth(p);
         int s = 0, issued = 0;
-        uint32_t ph = 0;
         for (int k = 0; k < units; ++k) {
-            if (k >= stages && !mbar_wait(smem_u32(empty + s), ph ^ 1u)) break;
+            if (!ring_slot_ready(empty, k, stages, depth)) break;
             const int row = r0 + k * rs;
             const int ru = min(rs, r1 - row);
             const uint32_t bytes = uint32_t(ru) * uint32_t(cols) * 2u;
@@ -641,7 +658,7 @@ __device__ __forceinline__ bool rbulk_stream(const Params& p, unsigned char* sme
             bulk_copy_g2s(smem_u32(dst), p.w + goff, bytes, fb, pol);
             if constexpr (GATED) bulk_copy_g2s(smem_u32(dst + size_t(rs) * cols), p.u + goff, bytes, fb, pol);
             ++issued;
-            if (++s == stages) { s = 0; ph ^= 1u; }
+            if (++s == stages) s = 0;
         }
         SWB_TIMELINE(4);
         const int drain = issued < stages ? issued : stages;

@@ -182,6 +182,18 @@ struct Launcher<SWB_FAM_BULK, W, R, PK, U, CH, ST> {
     }
 };
 
+// Copies a BULK / RBULK producer keeps in flight once its ring is full: enough
+// for about SWB_INFLIGHT_TARGET bytes per SM (at least two, at most the ring).
+// The first ring-full still goes out at once. 0 keeps the whole ring in flight.
+#ifndef SWB_INFLIGHT_TARGET
+#define SWB_INFLIGHT_TARGET 0
+#endif
+int inflight_cap(size_t stage_bytes, int cps, int stages) {
+    if (SWB_INFLIGHT_TARGET <= 0 || stage_bytes == 0) return 0;
+    const int d = int(size_t(SWB_INFLIGHT_TARGET) / (size_t(cps) * stage_bytes));
+    return std::min(stages, std::max(2, d));
+}
+
 template <int CW, int CPS, int CH, int ST, int MODE>
 int launch_bulk(Params p, cudaStream_t stream, bool pdl) {
     constexpr int NM = MODE == MODE_GATE ? 2 : 1;
@@ -197,6 +209,7 @@ int launch_bulk(Params p, cudaStream_t stream, bool pdl) {
     while (stages >= 2 && bulk_layout(NM, CH, stages, p.cols, CW, rows_per_cta).total > budget) --stages;
     if (!aligned || stages < 2) return run_fallback<MODE>(p, stream, pdl);
     p.stages = stages;
+    p.inflight = inflight_cap(size_t(NM) * CH * 2, CPS, stages);
     p.x_staged = 1;
     const size_t smem = bulk_layout(NM, CH, stages, p.cols, CW, rows_per_cta).total;
     auto kernel = bulk_kernel<CW, CH, MODE>;
@@ -231,6 +244,7 @@ int launch_rbulk(Params p, cudaStream_t stream, bool pdl) {
     // memory for the next kernel's CTAs to become resident early
     stages = std::min(stages, std::max(2, (rows_per_cta + rs - 1) / rs));
     p.stages = stages;
+    p.inflight = inflight_cap(size_t(rs) * row_bytes, CPS, stages);
     p.row_stage = rs;
     const size_t smem = rbulk_layout(NM, rs, p.cols, stages, CW, rows_per_cta).total;
     auto kernel = rbulk_kernel<CW, MAXJ, CPS, MODE>;
@@ -267,6 +281,7 @@ int launch_rbulk_ar(Params p, const TpParams& tp, cudaStream_t stream, bool pdl)
     if (rs < 1 || stages < 2) return fail(SWB_E_UNSUPPORTED, "shape does not fit the geometry's shared memory");
     stages = std::min(stages, std::max(2, (rows_per_cta + rs - 1) / rs));  // as launch_rbulk
     p.stages = stages;
+    p.inflight = inflight_cap(size_t(rs) * row_bytes, CPS, stages);
     p.row_stage = rs;
     const size_t smem = rbulk_layout(1, rs, p.cols, stages, CW, rows_per_cta).total;
     auto kernel = rbulk_allreduce_kernel<CW, MAXJ, CPS, HALF>;

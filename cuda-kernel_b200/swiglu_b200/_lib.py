@@ -17,6 +17,7 @@ REPO_ROOT = PKG_ROOT.parent
 LIB_DIR = PKG_ROOT / "lib"
 LIB_PATH = LIB_DIR / "libswiglu_b200.so"
 CUBLAS_LIB_PATH = LIB_DIR / "libswiglu_b200_cublas.so"
+TIMELINE_LIB_PATH = LIB_DIR / "libswiglu_b200_timeline.so"   # measurement build (make timeline)
 HEADERS = [REPO_ROOT / "include" / "swiglu_b200.h", REPO_ROOT / "include" / "swiglu_b200_cublas.h"]
 
 # status codes (include/swiglu_b200.h)
@@ -157,6 +158,19 @@ def cublas_lib() -> ctypes.CDLL:
                     raise NativeLibraryMissing(f"{CUBLAS_LIB_PATH} is missing: build it with `make -C {PKG_ROOT}`")
                 _cublas = _declare_cublas(ctypes.CDLL(str(CUBLAS_LIB_PATH)))
     return _cublas
+
+
+def timeline_lib(path=None) -> ctypes.CDLL:
+    """The timeline measurement build (``make timeline``): the product's C ABI plus
+    swb_timeline_reset/read/capacity. Used only by swiglu_b200.timeline."""
+    path = Path(path) if path else TIMELINE_LIB_PATH
+    if not path.exists():
+        raise NativeLibraryMissing(f"{path} is missing: build it with `make -C {PKG_ROOT} timeline`")
+    L = _declare(ctypes.CDLL(str(path)))
+    L.swb_timeline_reset.argtypes, L.swb_timeline_reset.restype = [], _i
+    L.swb_timeline_read.argtypes, L.swb_timeline_read.restype = [_vp, ctypes.POINTER(ctypes.c_uint)], _i
+    L.swb_timeline_capacity.argtypes, L.swb_timeline_capacity.restype = [], _i
+    return L
 
 
 def status_message(status: int) -> str:
