@@ -691,17 +691,52 @@ def ours(args) -> None:
                "d2h_bytes_per_step": world * H * 4,
                "path": "every rank: pinned host x -> H2D -> captured swb_ffn_tp_fused (C ABI) -> D2H -> pinned host y"}
     if world == 1:
-        x_host = common["x"].cpu().pin_memory()
-        y_host = torch.empty(H, dtype=torch.float32).pin_memory()
+        # The reference's transfer-inclusive protocol (src/benchmark.cu:177-206): every step
+        # copies its x in from page-locked host memory, runs the layer and copies y back out,
+        # steps back to back in one stream. Through swb_ffn_host_ex (binding.ffn_host): the
+        # transfers are kernels in the layer's programmatic chain, so with SWB_PREFETCH_WEIGHTS
+        # the next step's gate streams its weights while this step's y and the next x cross
+        # PCIe. `chain` steps per CUDA graph as above, each step with its own pinned x and y.
+        n_host = max(chain, 1)
+        x_hosts = [(common["x"].float() * (1.0 + 0.01 * k)).half().cpu().pin_memory() for k in range(n_host)]
+        y_hosts = [torch.empty(H, dtype=torch.float32).pin_memory() for _ in range(n_host)]
         x_dev = torch.empty_like(x)
+
+        def host_step(k):
+            s = sets[k % copies]
+            binding.ffn_host(x_hosts[k], s["wg"], s["wu"], s["wd"], bg, bu, bd, x_dev, h, y, y_hosts[k], gcfg,
+                             dcfg, stream=sp, prefetch_weights=True)
+
+        for k in range(n_host):
+            host_step(k)
+        torch.cuda.synchronize()
+        hg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(hg, stream=stream):
+            for k in range(n_host):
+                host_step(k)
+        for _ in range(max(args.warmup, 3)):
+            hg.replay()
+        torch.cuda.synchronize()
+        reps = max(1, args.steps // n_host)
+        e2e_us = time_kernel(torch, lambda i: hg.replay(), reps, stream) / n_host
+        hg.reset()
+        del hg
+        # every step's host y against the device-buffer layer on that step's x
+        for k in range(n_host):
+            s = sets[k % copies]
+            binding.ffn(x_hosts[k].to(device), s["wg"], s["wu"], s["wd"], bg, bu, bd, h, y, gcfg, dcfg, stream=sp)
+            torch.cuda.synchronize()
+            if not torch.equal(y_hosts[k], y.cpu()):
+                raise SystemExit(f"end-to-end output mismatch at step {k}")
+
+        # beside it, the one-step-per-graph protocol with copy operations: pinned x -> H2D ->
+        # captured swb_ffn (C ABI) -> D2H -> pinned y, one graph replay per step
+        x_host, y_host = x_hosts[0], y_hosts[0]
         e2e_graphs = []
+
         def public_call(c):
-            if lcfg:
-                binding.ffn_fused(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, lcfg,
-                                  workspace, stream=sp)
-            else:
-                binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg,
-                            stream=sp)
+            binding.ffn(x_dev, sets[c]["wg"], sets[c]["wu"], sets[c]["wd"], bg, bu, bd, h, y, gcfg, dcfg,
+                        stream=sp)
 
         for c in range(copies):
             public_call(c)
@@ -720,15 +755,19 @@ def ours(args) -> None:
         for i in range(max(args.warmup, 3)):
             e2e_step(i)
         torch.cuda.synchronize()
-        e2e_us = time_kernel(torch, e2e_step, args.steps, stream)
-        if not torch.equal(y_host, y.cpu()):
-            raise SystemExit("end-to-end output mismatch")
-        e2e = {"value": e2e_us, "unit": UNIT,
-               "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
-               "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
-               "path": "pinned host x -> H2D -> captured %s (C ABI) -> D2H -> pinned host y"
-                       % ("swb_ffn_fused" if lcfg else "swb_ffn")}
+        copy_us = time_kernel(torch, e2e_step, args.steps, stream)
+        for g in e2e_graphs:
+            g.reset()
         del e2e_graphs
+        e2e = {"value": e2e_us, "unit": UNIT,
+               "h2d_bytes_per_step": x_hosts[0].numel() * x_hosts[0].element_size(),
+               "d2h_bytes_per_step": y_hosts[0].numel() * y_hosts[0].element_size(),
+               "path": f"pinned host x -> swb_ffn_host_ex (C ABI: x in, gate, down, y out as one programmatic "
+                       f"chain, SWB_PREFETCH_WEIGHTS) -> pinned host y; {n_host} steps per CUDA graph, "
+                       f"each with its own pinned x and y; every step's y checked against swb_ffn",
+               "one_step_copy_graph_us": copy_us,
+               "one_step_copy_graph_path": "pinned x -> H2D copy -> one captured swb_ffn per graph replay -> D2H "
+                                           "copy -> pinned y"}
 
     # ---- cuBLAS GemmEx + pointwise on the same GPU (baseline, N=1)
     cublas = None

@@ -1136,4 +1136,28 @@ __global__ void residual_epilogue_kernel(float* y, const __half* bias, const __h
     if (i < n) y[i] += __half2float(bias[i]) + __half2float(x[i]);
 }
 
+// ===================================================== host-buffer transfers
+
+// One step of a layer call from page-locked host x to page-locked host y
+// (swb_ffn_host_ex): x in, or y out, over PCIe. The transfers are kernels, not
+// copy operations, so consecutive calls stay one chain of programmatic launches:
+// the next call's gate streams its weights while this call's y and the next x
+// cross the bus. `src` / `dst` may be the device address of page-locked host
+// memory (unified addressing). The loads are plain (not the read-only path): the
+// host rewrites its buffer between calls. 16-byte pieces when both ends are
+// 16-byte aligned, bytes otherwise.
+__global__ void transfer_kernel(const unsigned char* src, unsigned char* dst, size_t bytes) {
+    griddep_launch_dependents();
+    griddep_wait();  // the previous kernel of the chain has finished with dst (or written src)
+    const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t n = size_t(gridDim.x) * blockDim.x;
+    size_t done = 0;
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        const size_t pieces = bytes / 16;
+        for (size_t i = t; i < pieces; i += n) reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+        done = pieces * 16;
+    }
+    for (size_t i = done + t; i < bytes; i += n) dst[i] = src[i];
+}
+
 }  // namespace swb

@@ -599,6 +599,41 @@ Params make_params() {
     return p;
 }
 
+// The device address of page-locked host memory this device maps (every
+// cudaHostAlloc / cudaHostRegister buffer under unified addressing), or null for
+// anything else -- pageable or device memory is rejected before any launch.
+const void* mapped_host(const void* p) {
+    cudaPointerAttributes a;
+    std::memset(&a, 0, sizeof a);
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
+// transfer_kernel over `bytes`: 256 threads per CTA, one 16-byte piece per thread,
+// at most one CTA per SM. pdl: launched programmatically after the previous kernel.
+int launch_transfer(const void* src, void* dst, size_t bytes, cudaStream_t stream, bool pdl) {
+    const int sms = sm_count();
+    if (sms <= 0) return check_launch();
+    const size_t pieces = (bytes + 15) / 16;
+    const unsigned block = 256;
+    const unsigned grid = unsigned(std::max<size_t>(1, std::min<size_t>(size_t(sms), (pieces + block - 1) / block)));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, transfer_kernel, static_cast<const unsigned char*>(src), static_cast<unsigned char*>(dst),
+                       bytes);
+    return check_launch();
+}
+
 }  // namespace
 }  // namespace swb
 
@@ -739,6 +774,30 @@ int swb_ffn_ex(int gate_config, int down_config, const void* wg, const void* wu,
                            (flags & SWB_PREFETCH_WEIGHTS) != 0))
         return rc;
     return project_impl(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream, true);
+}
+
+int swb_ffn_host_ex(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
+                    const void* x_host, const void* bg, const void* bu, const void* bd, void* x, void* h, float* y,
+                    float* y_host, int hidden, int inter, unsigned flags, void* stream) {
+    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
+    if (!find_config(gate_config) || !find_config(down_config)) return fail(SWB_E_CONFIG);
+    if (hidden <= 0 || inter <= 0 || !wg || !wd || !x_host || !x) return fail(SWB_E_INPUT);
+    if (!wu || !h) return fail(SWB_E_GATE_BUFFERS);
+    if (!y || !y_host) return fail(SWB_E_FLOAT_OUTPUT);
+    const size_t xb = size_t(hidden) * 2, hb = size_t(inter) * 2, yb = size_t(hidden) * 4;
+    if (overlaps(x, xb, h, hb) || overlaps(x, xb, y, yb) || overlaps(h, hb, y, yb)) return fail(SWB_E_OVERLAP_OUTPUT);
+    const void* xs = mapped_host(x_host);
+    void* yd = const_cast<void*>(mapped_host(y_host));
+    if (!xs || !yd)
+        return fail(SWB_E_INPUT, "x_host and y_host must be page-locked host memory mapped for this device "
+                                 "(cudaHostAlloc or cudaHostRegister)");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // x in; without SWB_PREFETCH_WEIGHTS after everything before the call has finished
+    if (int rc = launch_transfer(xs, x, xb, s, (flags & SWB_PREFETCH_WEIGHTS) != 0)) return rc;
+    // the gate may stream its weights while x crosses the bus (the transfer writes no weight)
+    if (int rc = gate_impl(gate_config, wg, wu, x, bg, bu, h, inter, hidden, 0, stream, nullptr, true)) return rc;
+    if (int rc = project_impl(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream, true)) return rc;
+    return launch_transfer(y, yd, yb, s, true);  // y out
 }
 
 int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, const void* wu_shard, const void* wd_shard,

@@ -146,6 +146,29 @@ def ffn(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, b
                                          y.data_ptr(), hidden, inter, flags, s))
 
 
+def ffn_host(x_host: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, bg: torch.Tensor,
+             bu: torch.Tensor, bd: torch.Tensor, x: torch.Tensor, h: torch.Tensor, y: torch.Tensor,
+             y_host: torch.Tensor, gate_config: int, down_config: int, stream: int | None = None,
+             prefetch_weights: bool = False) -> None:
+    """The layer from pinned host ``x_host`` (fp16 [H]) to pinned host ``y_host`` (fp32 [H])
+    (swb_ffn_host_ex): x in, gate, down, y out as one programmatic chain on the GPU. ``x``,
+    ``h`` and ``y`` are device buffers the call overwrites. ``y_host`` holds the result once
+    the stream has passed the call. ``prefetch_weights``: consecutive calls form one chain."""
+    inter, hidden = wg.shape
+    _check(x_host.device.type == "cpu" and y_host.device.type == "cpu", "x_host and y_host must be host tensors")
+    _check(x_host.is_pinned() and y_host.is_pinned(), "x_host and y_host must be pinned (page-locked)")
+    _check(x_host.dtype == torch.float16 and y_host.dtype == torch.float32, "x_host fp16, y_host fp32")
+    _check(x_host.numel() == hidden and y_host.numel() == hidden and x_host.is_contiguous()
+           and y_host.is_contiguous(), "x_host and y_host must be contiguous [hidden]")
+    s = _stream(x.device) if stream is None else stream
+    flags = _lib.SWB_PREFETCH_WEIGHTS if prefetch_weights else 0
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().swb_ffn_host_ex(int(gate_config), int(down_config), wg.data_ptr(), wu.data_ptr(),
+                                              wd.data_ptr(), x_host.data_ptr(), _ptr(bg), _ptr(bu), _ptr(bd),
+                                              x.data_ptr(), h.data_ptr(), y.data_ptr(), y_host.data_ptr(), hidden,
+                                              inter, flags, s))
+
+
 def layer_config_ids() -> list[int]:
     """Ids of the fused whole-layer kernels (swb_ffn_fused)."""
     L = _lib.lib()

@@ -232,6 +232,21 @@ SWB_API int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, 
                                 const void* bu_shard, const void* bd, void* h_shard, float* y, int hidden, int shard,
                                 unsigned flags, void* stream);
 
+/* The layer from host x to host y: the reference's transfer-inclusive step,
+ * src/benchmark.cu:177-206 (copy x in, layer, copy y out, steps back to back in
+ * one stream), as one call. x_host [hidden] fp16 and y_host [hidden] fp32 must be
+ * page-locked host memory this device maps (cudaHostAlloc / cudaHostRegister;
+ * anything else: SWB_E_INPUT before any launch). x [hidden] fp16, h [inter] fp16
+ * and y [hidden] fp32 are device buffers the call overwrites. The transfers run as
+ * kernels chained programmatically with the gate and down kernels, so the gate
+ * streams Wg/Wu while x crosses the bus, and with SWB_PREFETCH_WEIGHTS (same
+ * promise as above) consecutive calls form one chain: the next call's gate streams
+ * its weights while this call's y and the next x cross. y_host holds the result
+ * once the stream has passed the call. No counterpart in the reference. */
+SWB_API int swb_ffn_host_ex(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
+                            const void* x_host, const void* bg, const void* bu, const void* bd, void* x, void* h,
+                            float* y, float* y_host, int hidden, int inter, unsigned flags, void* stream);
+
 /* swiglu_out, src/torch_extension.cu:7-40: the binding's shape / config / alias guards,
  * then the model-rounding gate into h [inter] and the fp16 down projection into
  * y [hidden] (no bias, no residual -- the residual stays in the transformer layer).

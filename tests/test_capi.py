@@ -218,6 +218,35 @@ def test_tp_model_path_and_epoch_guards_without_gpu():
     assert L().swb_tp_epoch(FAKE, None) == _lib.SWB_E_INPUT
 
 
+def test_host_buffer_layer_guards_without_gpu():
+    """swb_ffn_host_ex refuses unknown flags, invalid geometries, missing or aliased buffers and
+    host pointers that are not page-locked host memory -- all before any launch."""
+    f = L().swb_ffn_host_ex
+    x, h, y = 0x7F0000100000, 0x7F0000200000, 0x7F0000300000
+
+    def call(g=69, d=101, wg=FAKE, wu=FAKE, wd=FAKE, xh=FAKE, xd=x, hd=h, yd=y, yh=FAKE, hidden=64, inter=96,
+             flags=0):
+        return f(g, d, wg, wu, wd, xh, None, None, None, xd, hd, yd, yh, hidden, inter, flags, None)
+
+    assert call(flags=2) == _lib.SWB_E_INPUT
+    assert b"flags" in L().swb_last_error()
+    assert call(g=999) == _lib.SWB_E_CONFIG
+    assert call(d=0) == _lib.SWB_E_CONFIG
+    assert call(xh=None) == _lib.SWB_E_INPUT
+    assert call(xd=None) == _lib.SWB_E_INPUT
+    assert call(hidden=0) == _lib.SWB_E_INPUT
+    assert call(wu=None) == _lib.SWB_E_GATE_BUFFERS
+    assert call(hd=None) == _lib.SWB_E_GATE_BUFFERS
+    assert call(yd=None) == _lib.SWB_E_FLOAT_OUTPUT
+    assert call(yh=None) == _lib.SWB_E_FLOAT_OUTPUT
+    assert call(hd=x + 64) == _lib.SWB_E_OVERLAP_OUTPUT          # h inside x's 128 bytes
+    assert call(yd=h + 100) == _lib.SWB_E_OVERLAP_OUTPUT         # y inside h's 192 bytes
+    # not page-locked host memory (here: not memory at all): refused on the host
+    assert call() == _lib.SWB_E_INPUT
+    assert b"page-locked" in L().swb_last_error()
+    assert call(flags=_lib.SWB_PREFETCH_WEIGHTS) == _lib.SWB_E_INPUT
+
+
 C_CALLER = r"""
 #include <stdio.h>
 #include <string.h>
