@@ -670,9 +670,48 @@ def ours(args) -> None:
     # x from pinned host memory, runs the captured layer call, copies y back to pinned host.
     e2e = None
     if world > 1:
-        # every rank: pinned H2D of x, the captured layer step, D2H of y (max over ranks)
-        x_host = x.cpu().pin_memory()
-        y_host = torch.empty(H, dtype=torch.float32).pin_memory()
+        # Every rank: the reference's transfer-inclusive step (src/benchmark.cu:177-206) through
+        # swb_ffn_tp_host_ex -- x in from page-locked host memory (the same x on every rank), the
+        # rank's gate and fused down + exchange, the reduced y out to page-locked host memory --
+        # `chain` steps per CUDA graph as for `value`, each step with its own pinned x and y,
+        # max over ranks. Beside it, one step per graph with copy operations.
+        from swiglu_b200 import tp as T
+        n_host = max(chain, 1)
+        x_hosts = [(x.float() * (1.0 + 0.01 * k)).half().cpu().pin_memory() for k in range(n_host)]
+        y_hosts = [torch.empty(H, dtype=torch.float32).pin_memory() for _ in range(n_host)]
+        x_dev = torch.empty_like(x)
+        g_id, d_id = (lcfg, 0) if lcfg else (gcfg, dcfg)
+
+        def rank_shard(k):
+            s = sets[k % copies]
+            return {"wg": s["wg"], "wu": s["wu"], "wd": s["wd"], "bg": bg, "bu": bu}
+
+        def host_step(k):
+            T.ffn_tp_host(exchange, x_hosts[k], rank_shard(k), bd, x_dev, h, y, y_hosts[k], g_id, d_id, stream=sp,
+                          prefetch_weights=True)
+
+        for k in range(n_host):
+            host_step(k)
+        torch.cuda.synchronize()
+        hg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(hg, stream=stream):
+            for k in range(n_host):
+                host_step(k)
+        for _ in range(max(args.warmup, 3)):
+            hg.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        reps = max(1, args.steps // n_host)
+        e2e_us = time_kernel(torch, lambda i: hg.replay(), reps, stream) / n_host
+        hg.reset()
+        del hg
+        # every step's host y against the device-buffer call on that step's x (all ranks agree)
+        bad = 0
+        for k in range(n_host):
+            T.ffn_tp_fused(exchange, x_hosts[k].to(device), rank_shard(k), bd, h, y, g_id, d_id, stream=sp)
+            torch.cuda.synchronize()
+            bad += int(not torch.equal(y_hosts[k], y.cpu()))
+        x_host, y_host = x_hosts[0], y_hosts[0]
         x_keep = x.clone()
 
         def e2e_step_tp(i):
@@ -683,13 +722,21 @@ def ours(args) -> None:
         for i in range(max(args.warmup, 3)):
             e2e_step_tp(i)
         dist.barrier()
-        e2e_us = time_kernel(torch, e2e_step_tp, args.steps, stream)
-        t = torch.tensor([e2e_us], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        copy_us = time_kernel(torch, e2e_step_tp, args.steps, stream)
         x.copy_(x_keep)
-        e2e = {"value": float(t.item()), "unit": UNIT, "h2d_bytes_per_step": world * H * 2,
+        t = torch.tensor([e2e_us, copy_us, bad], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if t[2].item() > 0:
+            raise SystemExit("end-to-end output mismatch on some rank")
+        e2e = {"value": float(t[0]), "unit": UNIT, "h2d_bytes_per_step": world * H * 2,
                "d2h_bytes_per_step": world * H * 4,
-               "path": "every rank: pinned host x -> H2D -> captured swb_ffn_tp_fused (C ABI) -> D2H -> pinned host y"}
+               "path": f"every rank: pinned host x -> swb_ffn_tp_host_ex (C ABI: x in, gate, fused down + "
+                       f"exchange, y out as one programmatic chain, SWB_PREFETCH_WEIGHTS) -> pinned host y; "
+                       f"{n_host} steps per CUDA graph, each with its own pinned x and y; every step's y checked "
+                       f"against swb_ffn_tp_fused_ex",
+               "one_step_copy_graph_us": float(t[1]),
+               "one_step_copy_graph_path": "every rank: pinned x -> H2D copy -> one captured swb_ffn_tp_fused per "
+                                           "graph replay -> D2H copy -> pinned y"}
     if world == 1:
         # The reference's transfer-inclusive protocol (src/benchmark.cu:177-206): every step
         # copies its x in from page-locked host memory, runs the layer and copies y back out,

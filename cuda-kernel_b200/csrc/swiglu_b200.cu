@@ -1021,21 +1021,16 @@ int swb_ffn_tp_fused(swb_tp_t* tp, int gate_config, int down_config, const void*
                                h_shard, y, hidden, shard, 0u, stream);
 }
 
-int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
-                        const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard,
-                        const void* bd, void* h_shard, float* y, int hidden, int shard, unsigned flags,
-                        void* stream) {
-    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
-    if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev != tp->device)
-        return fail(SWB_E_INPUT, "the current device is not the exchange's device");
-    if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
-    const bool layer = is_layer_config(gate_config);
-    if (!layer && (!find_config(gate_config) || !find_config(down_config))) return fail(SWB_E_CONFIG);
-    if (!wd_shard || !x) return fail(SWB_E_INPUT);
-    if (!y) return fail(SWB_E_FLOAT_OUTPUT);
-    if (layer) {  // one persistent kernel: gate, grid barrier, down + exchange
+namespace swb {
+namespace {
+// The rank's layer with the fused exchange, after the entry points' guards: a
+// whole-layer id (gate_config 200+) as one persistent kernel, else the gate (which
+// advances the call epoch) and the fused down + exchange kernel. pdl: the gate, or
+// a streaming whole-layer kernel, is launched programmatically.
+int tp_fused_launch(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
+                    const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard, const void* bd,
+                    void* h_shard, float* y, int hidden, int shard, bool pdl, cudaStream_t stream) {
+    if (is_layer_config(gate_config)) {  // one persistent kernel: gate, grid barrier, down + exchange
         if (!wg_shard || !wu_shard || !h_shard) return fail(SWB_E_GATE_BUFFERS);
         LayerParams L;
         std::memset(&L, 0, sizeof L);
@@ -1050,13 +1045,12 @@ int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const vo
         L.hidden = hidden;
         L.inter = shard;
         L.sync = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + kTpCounterBytes);
-        return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), static_cast<cudaStream_t>(stream),
-                                    (flags & SWB_PREFETCH_WEIGHTS) != 0);
+        return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), stream, pdl);
     }
     const TpParams t = tp_params(tp, bd, x);
     // the gate kernel advances the call epoch; the down kernel reads it after griddepcontrol.wait
     if (int rc = gate_impl(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream,
-                           t.ctr, (flags & SWB_PREFETCH_WEIGHTS) != 0))
+                           t.ctr, pdl))
         return rc;
     Params p = make_params();
     p.w = static_cast<const __half*>(wd_shard);
@@ -1065,7 +1059,59 @@ int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const vo
     p.rows = hidden;
     p.cols = shard;
     p.epoch = t.ctr;
-    return dispatch_allreduce(down_config, p, t, static_cast<cudaStream_t>(stream), true);
+    return dispatch_allreduce(down_config, p, t, stream, true);
+}
+
+// Guards shared by the fused tensor-parallel entry points.
+int tp_fused_guards(const swb_tp_t* tp, int gate_config, int down_config, const void* wd_shard, const void* x,
+                    const float* y, int hidden, unsigned flags) {
+    if (flags & ~SWB_PREFETCH_WEIGHTS) return fail(SWB_E_INPUT, "unknown launch flags");
+    if (!tp || !tp->connected) return fail(SWB_E_INPUT, "exchange missing or not connected");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != tp->device)
+        return fail(SWB_E_INPUT, "the current device is not the exchange's device");
+    if (hidden != tp->rows) return fail(SWB_E_SHAPE, "hidden differs from the exchange's rows");
+    if (!is_layer_config(gate_config) && (!find_config(gate_config) || !find_config(down_config)))
+        return fail(SWB_E_CONFIG);
+    if (!wd_shard || !x) return fail(SWB_E_INPUT);
+    if (!y) return fail(SWB_E_FLOAT_OUTPUT);
+    return SWB_OK;
+}
+}  // namespace
+}  // namespace swb
+
+int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
+                        const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard,
+                        const void* bd, void* h_shard, float* y, int hidden, int shard, unsigned flags,
+                        void* stream) {
+    if (int rc = tp_fused_guards(tp, gate_config, down_config, wd_shard, x, y, hidden, flags)) return rc;
+    return tp_fused_launch(tp, gate_config, down_config, wg_shard, wu_shard, wd_shard, x, bg_shard, bu_shard, bd,
+                           h_shard, y, hidden, shard, (flags & SWB_PREFETCH_WEIGHTS) != 0,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int swb_ffn_tp_host_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
+                       const void* wd_shard, const void* x_host, const void* bg_shard, const void* bu_shard,
+                       const void* bd, void* x, void* h_shard, float* y, float* y_host, int hidden, int shard,
+                       unsigned flags, void* stream) {
+    if (int rc = tp_fused_guards(tp, gate_config, down_config, wd_shard, x, y, hidden, flags)) return rc;
+    if (!x_host || shard <= 0) return fail(SWB_E_INPUT);
+    if (!h_shard) return fail(SWB_E_GATE_BUFFERS);
+    if (!y_host) return fail(SWB_E_FLOAT_OUTPUT);
+    const size_t xb = size_t(hidden) * 2, hb = size_t(shard) * 2, yb = size_t(hidden) * 4;
+    if (overlaps(x, xb, h_shard, hb) || overlaps(x, xb, y, yb) || overlaps(h_shard, hb, y, yb))
+        return fail(SWB_E_OVERLAP_OUTPUT);
+    const void* xs = mapped_host(x_host);
+    void* yd = const_cast<void*>(mapped_host(y_host));
+    if (!xs || !yd)
+        return fail(SWB_E_INPUT, "x_host and y_host must be page-locked host memory mapped for this device "
+                                 "(cudaHostAlloc or cudaHostRegister)");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (int rc = launch_transfer(xs, x, xb, s, (flags & SWB_PREFETCH_WEIGHTS) != 0)) return rc;  // x in
+    if (int rc = tp_fused_launch(tp, gate_config, down_config, wg_shard, wu_shard, wd_shard, x, bg_shard, bu_shard,
+                                 bd, h_shard, y, hidden, shard, true, s))
+        return rc;
+    return launch_transfer(y, yd, yb, s, true);  // y out (every rank holds the same y)
 }
 
 int swb_swiglu_tp_out(swb_tp_t* tp, const void* x, const void* gate_shard, const void* up_shard,

@@ -108,6 +108,7 @@ def _declare(L: ctypes.CDLL) -> ctypes.CDLL:
         "swb_ffn_tp_fused": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, _vp], _i),
         "swb_ffn_tp_fused_ex": ([_vp, _i, _i] + [_vp] * 9 + [_i, _i, ctypes.c_uint, _vp], _i),
         "swb_ffn_host_ex": ([_i, _i] + [_vp] * 11 + [_i, _i, ctypes.c_uint, _vp], _i),
+        "swb_ffn_tp_host_ex": ([_vp, _i, _i] + [_vp] * 11 + [_i, _i, ctypes.c_uint, _vp], _i),
         "swb_swiglu_tp_out": ([_vp] * 7 + [_i64] * 4 + [ctypes.c_uint, _vp], _i),
         "swb_gate_epilogue": ([_vp, _vp, _vp, _vp, _vp, _i, _vp], _i),
         "swb_residual_epilogue": ([_vp, _vp, _vp, _i, _vp], _i),

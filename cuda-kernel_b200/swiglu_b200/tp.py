@@ -109,6 +109,26 @@ def ffn_tp_fused(ex: Exchange, x: torch.Tensor, s: dict, bd: torch.Tensor | None
                                                   y.data_ptr(), hidden, shard_rows, flags, sp))
 
 
+def ffn_tp_host(ex: Exchange, x_host: torch.Tensor, s: dict, bd: torch.Tensor | None, x: torch.Tensor,
+                h: torch.Tensor, y: torch.Tensor, y_host: torch.Tensor, gate_config: int, down_config: int,
+                stream: int | None = None, prefetch_weights: bool = False) -> None:
+    """ffn_tp_fused from pinned host ``x_host`` (fp16 [hidden], the same on every rank) to pinned
+    host ``y_host`` (fp32 [hidden], the reduced y, the same on every rank) (swb_ffn_tp_host_ex):
+    x in, the rank's gate and fused down + exchange, y out as one programmatic chain. ``x``,
+    ``h`` and ``y`` are device buffers the call overwrites."""
+    shard_rows, hidden = s["wg"].shape
+    if not (x_host.is_pinned() and y_host.is_pinned()):
+        raise RuntimeError("x_host and y_host must be pinned (page-locked) host tensors")
+    sp = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    flags = _lib.SWB_PREFETCH_WEIGHTS if prefetch_weights else 0
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().swb_ffn_tp_host_ex(ex.handle, int(gate_config), int(down_config), s["wg"].data_ptr(),
+                                                 s["wu"].data_ptr(), s["wd"].data_ptr(), x_host.data_ptr(),
+                                                 ptr(s["bg"]), ptr(s["bu"]), ptr(bd), x.data_ptr(), h.data_ptr(),
+                                                 y.data_ptr(), y_host.data_ptr(), hidden, shard_rows, flags, sp))
+
+
 def swiglu_tp_out(ex: Exchange, x: torch.Tensor, s: dict, h: torch.Tensor, y: torch.Tensor, gate_config: int,
                   down_config: int, stream: int | None = None, prefetch_weights: bool = False) -> None:
     """``swiglu_out`` for one tensor-parallel rank (the model path): eager-fp16 rounding in the

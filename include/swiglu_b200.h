@@ -247,6 +247,16 @@ SWB_API int swb_ffn_host_ex(int gate_config, int down_config, const void* wg, co
                             const void* x_host, const void* bg, const void* bu, const void* bd, void* x, void* h,
                             float* y, float* y_host, int hidden, int inter, unsigned flags, void* stream);
 
+/* swb_ffn_tp_fused_ex from host x to host y, one tensor-parallel rank: x_host in
+ * (every rank passes the same x), the rank's gate and fused down + exchange, the
+ * reduced y out to y_host (the same y on every rank). Buffers and flags as
+ * swb_ffn_host_ex; gate_config may be a whole-layer id. No counterpart in the
+ * reference. */
+SWB_API int swb_ffn_tp_host_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard,
+                               const void* wu_shard, const void* wd_shard, const void* x_host, const void* bg_shard,
+                               const void* bu_shard, const void* bd, void* x, void* h_shard, float* y,
+                               float* y_host, int hidden, int shard, unsigned flags, void* stream);
+
 /* swiglu_out, src/torch_extension.cu:7-40: the binding's shape / config / alias guards,
  * then the model-rounding gate into h [inter] and the fp16 down projection into
  * y [hidden] (no bias, no residual -- the residual stays in the transformer layer).

@@ -216,6 +216,11 @@ def test_tp_model_path_and_epoch_guards_without_gpu():
     out = ctypes.c_uint32()
     assert L().swb_tp_epoch(None, ctypes.byref(out)) == _lib.SWB_E_INPUT
     assert L().swb_tp_epoch(FAKE, None) == _lib.SWB_E_INPUT
+    fh = L().swb_ffn_tp_host_ex
+    assert fh(None, 69, 102, *([FAKE] * 11), 4096, 512, 0, None) == _lib.SWB_E_INPUT
+    assert b"exchange" in L().swb_last_error()
+    assert fh(None, 69, 102, *([FAKE] * 11), 4096, 512, 8, None) == _lib.SWB_E_INPUT  # unknown flag bit
+    assert b"flags" in L().swb_last_error()
 
 
 def test_host_buffer_layer_guards_without_gpu():

@@ -209,6 +209,62 @@ def test_fused_tp_prefetch_chain_matches_plain(gcfg):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("gcfg,dcfg", [(69, 102), (69, 87), (220, 0), (200, 0)])
+def test_fused_tp_host_buffers_match_device_calls(gcfg, dcfg):
+    """swb_ffn_tp_host_ex (pinned host x in, the rank's fused layer, pinned host y out) gives
+    bit-identically the y of swb_ffn_tp_fused, one call at a time and chained with
+    SWB_PREFETCH_WEIGHTS in one CUDA graph, each step with its own host buffers (one-rank
+    exchange); pageable host memory is refused before any launch."""
+    from swiglu_b200 import _lib, binding
+    from swiglu_b200 import tp as T
+    H, I, n = 4096, 14336, 8
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    w = O.normal_workload(4, H, I)
+    s = T.shard(t(w["wg"]), t(w["wu"]), t(w["wd"]), t(w["bg"]), t(w["bu"]), 5, n)
+    bd = t(w["bd"])
+    ex = T.Exchange(0, 1, H, dev)
+    h = torch.empty(I // n, dtype=torch.float16, device=dev)
+    x = torch.empty(H, dtype=torch.float16, device=dev)
+    y = torch.empty(H, dtype=torch.float32, device=dev)
+    steps = 5
+    xs = [(torch.from_numpy(w["x"]).float() * (1 + 0.25 * k)).half().pin_memory() for k in range(steps)]
+    ys = [torch.empty(H, dtype=torch.float32).pin_memory() for _ in range(steps)]
+    ref = []
+    for k in range(steps):
+        T.ffn_tp_fused(ex, xs[k].to(dev), s, bd, h, y, gcfg, dcfg)
+        torch.cuda.synchronize()
+        ref.append(y.cpu().clone())
+    for k in range(steps):
+        T.ffn_tp_host(ex, xs[k], s, bd, x, h, y, ys[k], gcfg, dcfg)
+    torch.cuda.synchronize()
+    assert all(torch.equal(ys[k], ref[k]) for k in range(steps))
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for k in range(steps):
+                T.ffn_tp_host(ex, xs[k], s, bd, x, h, y, ys[k], gcfg, dcfg, stream=stream.cuda_stream,
+                              prefetch_weights=True)
+        for _ in range(3):
+            for yk in ys:
+                yk.fill_(float("nan"))
+            g.replay()
+            stream.synchronize()
+            assert all(torch.equal(ys[k], ref[k]) for k in range(steps))
+        g.reset()
+    pageable = torch.from_numpy(w["x"].copy())
+    rc = _lib.lib().swb_ffn_tp_host_ex(ex.handle, gcfg, dcfg, s["wg"].data_ptr(), s["wu"].data_ptr(),
+                                       s["wd"].data_ptr(), pageable.data_ptr(), s["bg"].data_ptr(),
+                                       s["bu"].data_ptr(), bd.data_ptr(), x.data_ptr(), h.data_ptr(), y.data_ptr(),
+                                       ys[0].data_ptr(), H, I // n, 0, None)
+    assert rc == _lib.SWB_E_INPUT
+    torch.cuda.synchronize()
+    assert binding.device_error() == 0
+    ex.close()
+
+
+@pytest.mark.gpu
 def test_model_path_rank_matches_swiglu_out_and_oracle():
     """swb_swiglu_tp_out on a one-rank exchange is the binding's swiglu_out (model rounding,
     fp16 y, no bias or residual) with the down projection's rows summed through the exchange:

@@ -74,6 +74,14 @@ def _rank_body(rank, world, hidden, inter, q, dev, dist, torch, O, binding):
         T.ffn_tp_fused(ex, x, s, bd, h, y, gate, down)  # 200+: the rank's whole layer in one kernel
         torch.cuda.synchronize()
         out.append(y.cpu().numpy().copy())
+    # from pinned host x to pinned host y (swb_ffn_tp_host_ex): the same reduced y on every rank
+    x_host = x.cpu().pin_memory()
+    xd = torch.empty_like(x)
+    for gate, down in ((69, 102), (220, 0)):
+        y_host = torch.empty(hidden, dtype=torch.float32).pin_memory()
+        T.ffn_tp_host(ex, x_host, s, bd, xd, h, y, y_host, gate, down)
+        torch.cuda.synchronize()
+        out.append(y_host.numpy().copy())
     # geometries switched back to back with no host synchronisation: every call keeps its own y
     seq = [(69, 80), (200, 0), (69, 87), (220, 0), (201, 0), (69, 83), (223, 0), (103, 102), (69, 80)] * 3
     ys = [torch.empty_like(y) for _ in seq]
