@@ -53,6 +53,7 @@ struct Params {
     int blocks;          // sbulk_kernel: number of row blocks (= grid size)
     int block_stride;    // sbulk_kernel: A in row_block = (cta * A) mod blocks, gcd(A, blocks) = 1
     int inflight;        // bulk_kernel / rbulk_kernel: copies in flight once the ring is full (0 = ring depth)
+    float* y_host;       // MODE_F32: y also stored here (mapped page-locked host memory), or null
     // Tensor-parallel exchange call epoch (null otherwise): the gate kernel of a
     // call advances it (advance_call_epoch); the fused down kernel reads it after
     // griddepcontrol.wait, so both kernels of the call agree on it.
@@ -108,10 +109,12 @@ __device__ __forceinline__ void write_row(const Params& p, int row, float a, flo
     } else {
         if (p.bias) a += __half2float(p.bias[row]);
         if (p.residual) a += __half2float(p.residual[row]);
-        if constexpr (MODE == MODE_F16)
+        if constexpr (MODE == MODE_F16) {
             p.h[row] = __float2half_rn(a);
-        else
+        } else {
             p.y[row] = a;
+            if (p.y_host) p.y_host[row] = a;  // over PCIe; consecutive threads write consecutive rows
+        }
     }
 }
 

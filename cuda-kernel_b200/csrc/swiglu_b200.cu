@@ -729,7 +729,7 @@ int swb_gate(int config, const void* wg, const void* wu, const void* x, const vo
 namespace {
 // swb_project with an optional programmatic dependent launch (see launch_kernel).
 int project_impl(int config, const void* w, const void* x, const void* bias, const void* residual, void* out,
-                 int rows, int cols, unsigned flags, void* stream, bool pdl) {
+                 int rows, int cols, unsigned flags, void* stream, bool pdl, float* y_host = nullptr) {
     if (rows <= 0 || cols <= 0 || !w || !x) return fail(SWB_E_INPUT);
     const bool half_out = (flags & SWB_HALF_OUT) != 0;
     if (!out) return fail(half_out ? SWB_E_HALF_OUTPUT : SWB_E_FLOAT_OUTPUT);
@@ -748,6 +748,7 @@ int project_impl(int config, const void* w, const void* x, const void* bias, con
         return dispatch<MODE_F16>(config, p, s, pdl);
     }
     p.y = static_cast<float*>(out);
+    p.y_host = y_host;
     return dispatch<MODE_F32>(config, p, s, pdl);
 }
 }  // namespace
@@ -796,8 +797,15 @@ int swb_ffn_host_ex(int gate_config, int down_config, const void* wg, const void
     if (int rc = launch_transfer(xs, x, xb, s, (flags & SWB_PREFETCH_WEIGHTS) != 0)) return rc;
     // the gate may stream its weights while x crosses the bus (the transfer writes no weight)
     if (int rc = gate_impl(gate_config, wg, wu, x, bg, bu, h, inter, hidden, 0, stream, nullptr, true)) return rc;
-    if (int rc = project_impl(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream, true)) return rc;
-    return launch_transfer(y, yd, yb, s, true);  // y out
+    // y out: the BULK, RBULK and SBULK down kernels store it to the host buffer in their epilogue as
+    // well (consecutive threads write consecutive rows); after an LDG down kernel, whose rows are
+    // written one thread each, a transfer kernel copies it
+    const swb_config_t* dc = find_config(down_config);
+    const bool fold = dc->family != SWB_FAM_LDG;
+    if (int rc = project_impl(down_config, wd, h, bd, x, y, hidden, inter, SWB_RESIDUAL, stream, true,
+                              fold ? static_cast<float*>(yd) : nullptr))
+        return rc;
+    return fold ? SWB_OK : launch_transfer(y, yd, yb, s, true);
 }
 
 int swb_ffn_tp(int gate_config, int down_config, const void* wg_shard, const void* wu_shard, const void* wd_shard,

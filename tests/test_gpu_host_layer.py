@@ -16,7 +16,7 @@ from swiglu_b200 import _lib, binding
 
 pytestmark = pytest.mark.gpu
 
-PAIRS = [(69, 101), (68, 87), (69, 100), (33, 83), (96, 92)]
+PAIRS = [(69, 101), (68, 87), (69, 100), (33, 83), (96, 92), (69, 33)]  # 33: LDG down, y out by a transfer kernel
 
 
 def _layer(hidden, inter, seed, dev):
