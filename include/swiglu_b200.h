@@ -237,12 +237,14 @@ SWB_API int swb_ffn_tp_fused_ex(swb_tp_t* tp, int gate_config, int down_config, 
  * one stream), as one call. x_host [hidden] fp16 and y_host [hidden] fp32 must be
  * page-locked host memory this device maps (cudaHostAlloc / cudaHostRegister;
  * anything else: SWB_E_INPUT before any launch). x [hidden] fp16, h [inter] fp16
- * and y [hidden] fp32 are device buffers the call overwrites. The transfers run as
- * kernels chained programmatically with the gate and down kernels, so the gate
- * streams Wg/Wu while x crosses the bus, and with SWB_PREFETCH_WEIGHTS (same
- * promise as above) consecutive calls form one chain: the next call's gate streams
- * its weights while this call's y and the next x cross. y_host holds the result
- * once the stream has passed the call. No counterpart in the reference. */
+ * and y [hidden] fp32 are device buffers the call overwrites. x comes in through a
+ * transfer kernel chained programmatically ahead of the gate, so the gate streams
+ * Wg/Wu while x crosses the bus; the down kernel stores y to y_host in its
+ * epilogue as well (BULK, RBULK and SBULK down geometries; after an LDG one a
+ * transfer kernel copies it). With SWB_PREFETCH_WEIGHTS (same promise as above)
+ * consecutive calls form one chain: the next call's gate streams its weights
+ * while this call's y and the next x cross. y_host holds the result once the
+ * stream has passed the call. No counterpart in the reference. */
 SWB_API int swb_ffn_host_ex(int gate_config, int down_config, const void* wg, const void* wu, const void* wd,
                             const void* x_host, const void* bg, const void* bu, const void* bd, void* x, void* h,
                             float* y, float* y_host, int hidden, int inter, unsigned flags, void* stream);
