@@ -782,6 +782,7 @@ struct TpParams {
     uint32_t* ctr;
     const __half* bias;      // added once after the sum (may be null)
     const __half* residual;  // added once after the sum (may be null)
+    float* y_host;           // fp32 y also stored here (mapped page-locked host memory), or null
     int rank;
     int world;
 };
@@ -836,6 +837,8 @@ __device__ __forceinline__ void tp_exchange_rows(const TpParams& tp, uint32_t ep
         if (tp.bias) add += __half2float(tp.bias[r0 + i]);
         if (tp.residual) add += __half2float(tp.residual[r0 + i]);
         store_out(y, r0 + i, acc + add);
+        if constexpr (std::is_same_v<Out, float>)
+            if (tp.y_host) tp.y_host[r0 + i] = acc + add;  // over PCIe, consecutive rows per warp
     }
 }
 

@@ -1037,7 +1037,10 @@ namespace {
 // a streaming whole-layer kernel, is launched programmatically.
 int tp_fused_launch(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard, const void* wu_shard,
                     const void* wd_shard, const void* x, const void* bg_shard, const void* bu_shard, const void* bd,
-                    void* h_shard, float* y, int hidden, int shard, bool pdl, cudaStream_t stream) {
+                    void* h_shard, float* y, int hidden, int shard, bool pdl, cudaStream_t stream,
+                    float* y_host = nullptr) {
+    TpParams t = tp_params(tp, bd, x);
+    t.y_host = y_host;  // the reduced y also stored to mapped host memory (swb_ffn_tp_host_ex)
     if (is_layer_config(gate_config)) {  // one persistent kernel: gate, grid barrier, down + exchange
         if (!wg_shard || !wu_shard || !h_shard) return fail(SWB_E_GATE_BUFFERS);
         LayerParams L;
@@ -1053,9 +1056,8 @@ int tp_fused_launch(swb_tp_t* tp, int gate_config, int down_config, const void* 
         L.hidden = hidden;
         L.inter = shard;
         L.sync = reinterpret_cast<uint32_t*>(static_cast<char*>(tp->local) + tp->recv_bytes + kTpCounterBytes);
-        return dispatch_layer<true>(gate_config, L, tp_params(tp, bd, x), stream, pdl);
+        return dispatch_layer<true>(gate_config, L, t, stream, pdl);
     }
-    const TpParams t = tp_params(tp, bd, x);
     // the gate kernel advances the call epoch; the down kernel reads it after griddepcontrol.wait
     if (int rc = gate_impl(gate_config, wg_shard, wu_shard, x, bg_shard, bu_shard, h_shard, shard, hidden, 0, stream,
                            t.ctr, pdl))
@@ -1116,10 +1118,9 @@ int swb_ffn_tp_host_ex(swb_tp_t* tp, int gate_config, int down_config, const voi
                                  "(cudaHostAlloc or cudaHostRegister)");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (int rc = launch_transfer(xs, x, xb, s, (flags & SWB_PREFETCH_WEIGHTS) != 0)) return rc;  // x in
-    if (int rc = tp_fused_launch(tp, gate_config, down_config, wg_shard, wu_shard, wd_shard, x, bg_shard, bu_shard,
-                                 bd, h_shard, y, hidden, shard, true, s))
-        return rc;
-    return launch_transfer(y, yd, yb, s, true);  // y out (every rank holds the same y)
+    // y out: the exchange's epilogue stores the reduced rows to y_host as well (every rank the same y)
+    return tp_fused_launch(tp, gate_config, down_config, wg_shard, wu_shard, wd_shard, x, bg_shard, bu_shard, bd,
+                           h_shard, y, hidden, shard, true, s, static_cast<float*>(yd));
 }
 
 int swb_swiglu_tp_out(swb_tp_t* tp, const void* x, const void* gate_shard, const void* up_shard,

@@ -251,9 +251,9 @@ SWB_API int swb_ffn_host_ex(int gate_config, int down_config, const void* wg, co
 
 /* swb_ffn_tp_fused_ex from host x to host y, one tensor-parallel rank: x_host in
  * (every rank passes the same x), the rank's gate and fused down + exchange, the
- * reduced y out to y_host (the same y on every rank). Buffers and flags as
- * swb_ffn_host_ex; gate_config may be a whole-layer id. No counterpart in the
- * reference. */
+ * reduced y out to y_host (the same y on every rank), stored by the exchange's
+ * epilogue as it writes y. Buffers and flags as swb_ffn_host_ex; gate_config may
+ * be a whole-layer id. No counterpart in the reference. */
 SWB_API int swb_ffn_tp_host_ex(swb_tp_t* tp, int gate_config, int down_config, const void* wg_shard,
                                const void* wu_shard, const void* wd_shard, const void* x_host, const void* bg_shard,
                                const void* bu_shard, const void* bd, void* x, void* h_shard, float* y,
